@@ -1,0 +1,469 @@
+#!/usr/bin/env python3
+"""quillm-b200 benchmark: batch-1 greedy decode tok/s (+ matvec HBM GB/s, prefill) on N GPUs of one node.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload llama7b_q4_0|llama70b_q8_0|stories15m_q8_0]
+  python bench.py --impl reference ...      the reference's own CPU path (oracle/_ref) on this host's cores
+
+A step is one decode token.  The model (seeded N(0, 0.02) weights, synthesized in HBM) first consumes
+the workload's random prompt one token per step, then W untimed and K timed greedy decode steps run as
+a device-resident chain of CUDA-graph replays (value); `e2e` repeats K steps through the public
+per-token call with host buffers (token in, logits + next token out, copies inside the timed region).
+N > 1 (launched by torchrun): tensor parallelism over NCCL, timing = max over ranks, rank 0 prints.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 decode tok/s + matvec achieved HBM GB/s vs 8 TB/s peak"
+Q8_0, Q4_0 = 2, 3
+WORKLOADS = {
+    "llama7b_q4_0": dict(cfg=dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, n_kv_heads=32,
+                                  vocab_size=32000, max_seq=2048), dtype=Q4_0, seed=7, prompt=128,
+                         model="Llama-7B-shaped, Q4_0, N(0,0.02) seed 7"),
+    "llama70b_q8_0": dict(cfg=dict(dim=8192, hidden_dim=28672, n_layers=80, n_heads=64, n_kv_heads=8,
+                                   vocab_size=32000, max_seq=4096), dtype=Q8_0, seed=70, prompt=512,
+                          model="Llama-70B-shaped GQA, Q8_0, N(0,0.02) seed 70"),
+    "stories15m_q8_0": dict(cfg=dict(dim=288, hidden_dim=768, n_layers=6, n_heads=6, n_kv_heads=6,
+                                     vocab_size=32000, max_seq=256), dtype=Q8_0, seed=1, prompt=4,
+                            model="stories15M-shaped, Q8_0, N(0,0.02) seed 1"),
+}
+STD = 0.02
+DTYPE_NAME = {Q8_0: "q8_0", Q4_0: "q4_0"}
+
+
+def row_bytes(dt: int, n: int) -> int:
+    return ((n + 31) // 32) * (34 if dt == Q8_0 else 18)
+
+
+def prompt_ids(wl: dict) -> np.ndarray:
+    rng = np.random.default_rng(wl["seed"] + 1000)
+    return rng.integers(3, wl["cfg"]["vocab_size"], wl["prompt"]).astype(np.int32)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------ distributed plumbing
+class Dist:
+    """rank / world from torchrun's environment; torch.distributed only for id exchange, barriers and the
+    max-over-ranks timing reduction"""
+
+    def __init__(self, backend: str):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            kw = {}
+            if backend == "nccl":
+                import torch
+
+                kw["device_id"] = torch.device(f"cuda:{self.local}")
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=180), **kw)
+            self.pg = dist
+
+    def broadcast_bytes(self, b: bytes | None) -> bytes:
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def barrier(self):
+        if self.world > 1:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        import torch
+
+        dev = "cuda" if self.pg.get_backend() == "nccl" else "cpu"
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while running"""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", str(index)], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        rows = [[c.strip() for c in line.split(",")] for line in out.splitlines() if line.count(",") >= 7]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        busy = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ GPU arm
+def cuda_events(stream_ptr: int):
+    import torch
+
+    st = torch.cuda.ExternalStream(stream_ptr)
+    return st, torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def time_matvec(qb, torch, dt: int, rows: int, cols: int, iters: int = 60) -> tuple[float, float]:
+    """(seconds per launch, algorithmic bytes) of qmc_matvec, weights rotated over > 2x L2 of copies"""
+    rb = row_bytes(dt, cols)
+    wbytes = rows * rb
+    algo = wbytes + 4 * cols + 34 * ((cols + 31) // 32) + 4 * rows
+    copies = max(2, -(-256 * 2**20 // wbytes))
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + cols)
+    Ws = [torch.randint(0, 256, (wbytes + 256,), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+    # valid scales: write fp16 0.01 into every block's d so the arithmetic stays finite
+    for w in Ws:
+        v = w[:wbytes].view(rows, -1, 34 if dt == Q8_0 else 18)
+        v[:, :, 0] = 0x1F
+        v[:, :, 1] = 0x21
+    x = torch.randn(cols, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    xq = torch.empty(34 * ((cols + 31) // 32), dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()  # torch filled the inputs on its own stream
+    s = C.c_void_p()
+    qb.check(qb.cuda().qmc_stream(C.byref(s)))
+    st, e0, e1 = cuda_events(s.value)
+    for i in range(5):
+        qb.check(qb.cuda().qmc_matvec(dt, Ws[i % copies].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(),
+                                      xq.data_ptr(), None))
+    qb.check(qb.cuda().qmc_sync())
+    e0.record(st)
+    for i in range(iters):
+        qb.cuda().qmc_matvec(dt, Ws[i % copies].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(), xq.data_ptr(), None)
+    e1.record(st)
+    qb.check(qb.cuda().qmc_sync())
+    sec = e0.elapsed_time(e1) / 1e3 / iters
+    del Ws
+    return sec, float(algo)
+
+
+def time_prefill(qb, torch, T: int, N: int, K: int, iters: int = 10) -> float:
+    W = torch.randint(0, 256, (N * row_bytes(Q8_0, K) + 256,), dtype=torch.uint8, device="cuda")
+    v = W[: N * row_bytes(Q8_0, K)].view(N, -1, 34)
+    v[:, :, 0] = 0x1F
+    v[:, :, 1] = 0x21
+    A = torch.randn(T, K, device="cuda")
+    Cm = torch.empty(T, N, device="cuda")
+    torch.cuda.synchronize()
+    s = C.c_void_p()
+    qb.check(qb.cuda().qmc_stream(C.byref(s)))
+    st, e0, e1 = cuda_events(s.value)
+    qb.check(qb.cuda().qmc_matmul_nt_q(Q8_0, W.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, None))
+    qb.check(qb.cuda().qmc_sync())
+    e0.record(st)
+    for _ in range(iters):
+        qb.cuda().qmc_matmul_nt_q(Q8_0, W.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, None)
+    e1.record(st)
+    qb.check(qb.cuda().qmc_sync())
+    return e0.elapsed_time(e1) / 1e3 / iters
+
+
+def traffic_from_profiles(tag: str):
+    """DRAM bytes per launch recorded from an ncu capture (profiles/*.md line `traffic[<tag>] = <bytes>`)"""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for fn in sorted(os.listdir(pdir)):
+        if fn.endswith((".md", ".txt")):
+            for line in open(os.path.join(pdir, fn)):
+                if line.strip().startswith(f"traffic[{tag}]"):
+                    try:
+                        return float(line.split("=")[1].split()[0])
+                    except (IndexError, ValueError):
+                        pass
+    return None
+
+
+def gpu_arm(args, wl: dict) -> dict | None:
+    import torch
+
+    import quillm_b200 as qb
+
+    d = Dist("nccl")
+    torch.cuda.set_device(d.local)
+    qb.check(qb.cuda().qmc_set_device(d.local), "set_device")
+    cfg = dict(wl["cfg"])
+    nid = None
+    if d.world > 1:
+        buf = C.create_string_buffer(128)
+        if d.rank == 0:
+            qb.check(qb.cuda().qmc_nccl_unique_id(buf))
+        nid = d.broadcast_bytes(buf.raw if d.rank == 0 else None)
+    model = qb.Model(cfg, d.rank, d.world, nid)
+    model.synthesize(wl["dtype"], wl["seed"], STD)
+    prompt = prompt_ids(wl)
+    W, K = args.warmup, args.steps
+    npos = len(prompt)
+    if npos + W + 2 * K > cfg["max_seq"]:
+        raise SystemExit(f"{npos}+{W}+2*{K} positions exceed max_seq {cfg['max_seq']}")
+    s = C.c_void_p()
+    qb.check(qb.cuda().qmc_stream(C.byref(s)))
+    st, e0, e1 = cuda_events(s.value)
+
+    # prompt, one token per step like the reference (device-resident chain)
+    d.barrier()
+    qb.check(qb.cuda().qmc_sync())
+    e0.record(st)
+    first = int(model.generate(prompt, 1)[0])
+    e1.record(st)
+    qb.check(qb.cuda().qmc_sync())
+    prompt_s = d.max(e0.elapsed_time(e1) / 1e3)
+
+    clocks = ClockSampler(d.local)
+    model.enqueue_decode(first, npos, W)
+    qb.check(qb.cuda().qmc_sync())
+    pos0 = npos + W
+    d.barrier()
+    qb.check(qb.cuda().qmc_sync())
+    e0.record(st)
+    model.enqueue_decode(-1, 0, K)
+    e1.record(st)
+    qb.check(qb.cuda().qmc_sync())
+    d.barrier()
+    clk = clocks.stop()
+    sec = d.max(e0.elapsed_time(e1) / 1e3)
+    tok, pos = model.state()
+    assert pos == pos0 + K, (pos, pos0, K)
+
+    # e2e: the public per-token call, host buffers, copies inside the timed region
+    logits = np.zeros(cfg["vocab_size"], np.float32)
+    model.forward(tok, pos, logits)  # warm
+    d.barrier()
+    t0 = time.perf_counter()
+    t = tok
+    for i in range(K):
+        t = model.forward(t, pos + 1 + i, logits)
+    e2e_s = d.max(time.perf_counter() - t0)
+
+    per_gpu_bytes = np.mean([model.step_bytes(p) for p in range(pos0, pos0 + K)])
+    hbm, tflops, src = peaks()
+    step_time = sec / K
+    out = {
+        "metric": METRIC, "value": K / sec, "unit": "tok/s", "n_gpus": d.world, "steps": K, "warmup": W,
+        "ms_per_step": step_time * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "i8xi8->i32 dp4a, f32 scale/accumulate",
+        "data": f"synthetic: {wl['model']}; random prompt ids (numpy default_rng({wl['seed'] + 1000}))",
+        "config": {"workload": f"{args.workload}_decode", "model": wl["model"], "global_batch": 1,
+                   "seq_len": cfg["max_seq"], "prompt_tokens": npos, "decode_positions": [pos0, pos0 + K - 1],
+                   "parallelism": f"tp{d.world}",
+                   "l2": f"inputs larger than L2: {per_gpu_bytes / 1e9:.2f} GB streamed per step per GPU"},
+        "decode_roofline": {"bound": "hbm", "achieved": per_gpu_bytes / step_time / 1e9, "peak": hbm,
+                            "unit": "GB/s", "frac": per_gpu_bytes / step_time / 1e9 / hbm,
+                            "bytes_per_step_per_gpu": per_gpu_bytes, "peak_source": src},
+        "prompt_tok_s": npos / prompt_s,
+        "e2e": {"value": K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": cfg["vocab_size"] * 4 + 4},
+        "gpu_launches": K * (5 * cfg["n_layers"] + 3),
+        "clocks": clk,
+    }
+    model.close()
+    if d.rank == 0 and d.world == 1 and not args.quick:
+        out.update(kernel_sweeps(qb, torch, wl, hbm, tflops, src))
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args, wl)
+    d.close()
+    return out if d.rank == 0 else None
+
+
+def kernel_sweeps(qb, torch, wl: dict, hbm: float, tflops: float, src: str) -> dict:
+    """matvec sweep, the decode GEMV mix (roofline of the dominant kernel), prefill"""
+    res = {"matvec": []}
+    for dt in (Q4_0, Q8_0):
+        for rows, cols in ((4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096), (28672, 8192)):
+            sec, algo = time_matvec(qb, torch, dt, rows, cols)
+            res["matvec"].append({"shape": f"{rows}x{cols}", "dtype": DTYPE_NAME[dt], "us": sec * 1e6,
+                                  "GB/s": algo / sec / 1e9, "frac": algo / sec / 1e9 / hbm})
+    c = wl["cfg"]
+    D, H, V, L = c["dim"], c["hidden_dim"], c["vocab_size"], c["n_layers"]
+    kvd = D // c["n_heads"] * c["n_kv_heads"]
+    mix = [(D + 2 * kvd, D, L), (D, D, L), (2 * H, D, L), (D, H, L), (V, D, 1)]
+    tot_b = tot_t = 0.0
+    for rows, cols, n in mix:
+        sec, algo = time_matvec(qb, torch, wl["dtype"], rows, cols)
+        tot_b += n * algo
+        tot_t += n * sec
+    tag = f"{DTYPE_NAME[wl['dtype']]} decode mix"
+    traffic = traffic_from_profiles(f"gemv {DTYPE_NAME[wl['dtype']]} 11008x4096")
+    res["roofline"] = {"bound": "hbm", "kernel": f"gemv_q_kernel<{DTYPE_NAME[wl['dtype']].upper()}> ({tag})",
+                       "achieved": tot_b / tot_t / 1e9, "peak": hbm, "unit": "GB/s",
+                       "frac": tot_b / tot_t / 1e9 / hbm, "traffic": traffic,
+                       "traffic_note": "DRAM bytes per 11008x4096 launch from ncu (algorithmic 25.43 MB)",
+                       "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
+    res["prefill"] = []
+    for N, Kd in ((4096, 4096), (11008, 4096)):
+        for T in (1, 8, 32, 128, 512):
+            sec = time_prefill(qb, torch, T, N, Kd)
+            res["prefill"].append({"T": T, "N": N, "K": Kd, "tok/s": T / sec, "TFLOP/s": 2 * T * N * Kd / sec / 1e12,
+                                   "us": sec * 1e6})
+    return res
+
+
+# ------------------------------------------------------------------ CPU baseline / reference arm
+def model_file(wl: dict, name: str) -> str:
+    from oracle import oracle as O
+
+    d = os.environ.get("QUILLM_BENCH_DIR", "/tmp/quillm_bench")
+    os.makedirs(d, exist_ok=True)
+    path = os.path.join(d, f"{name}_seed{wl['seed']}.qlm")
+    if not os.path.exists(path + ".ok"):
+        O.synth_write(path, wl["cfg"], wl["dtype"], wl["seed"], STD, os.cpu_count())
+        open(path + ".ok", "w").close()
+    return path
+
+
+def ref_model(wl: dict, name: str, threads: int):
+    """the reference's best ISA on this host (AVX2 vs AVX-512, as its README recommends measuring)"""
+    from oracle import oracle as O
+
+    path = model_file(wl, name)
+    best = None
+    for isa in (O.ISA_AVX512, O.ISA_AVX2):
+        if not O.ref().ref_isa_supported(isa):
+            continue
+        m = O.RefModel(path, threads=threads, isa=isa, max_seq=wl["cfg"]["max_seq"])
+        m.forward(int(prompt_ids(wl)[0]), 0)
+        t0 = time.perf_counter()
+        m.forward(int(prompt_ids(wl)[1 % wl["prompt"]]), 1)
+        m.forward(int(prompt_ids(wl)[2 % wl["prompt"]]), 2)
+        dt = time.perf_counter() - t0
+        if best is None or dt < best[0]:
+            if best:
+                best[2].close()
+            best = (dt, isa, m)
+        else:
+            m.close()
+    if best is None:
+        m = O.RefModel(path, threads=threads, isa=O.ISA_SCALAR, max_seq=wl["cfg"]["max_seq"])
+        return m, O.ISA_SCALAR
+    return best[2], best[1]
+
+
+def cpu_baseline(args, wl: dict) -> dict:
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    m, isa = ref_model(wl, args.workload, threads)
+    prompt = prompt_ids(wl)
+    npre = min(4, len(prompt))
+    for p in range(npre):
+        lg = m.forward(int(prompt[p]), p)
+    tok = int(np.argmax(lg))
+    n, t0 = 0, time.perf_counter()
+    while n < 64 and (time.perf_counter() - t0 < 10.0 or n < 3):
+        tok = int(np.argmax(m.forward(tok, npre + n)))
+        n += 1
+    sec = time.perf_counter() - t0
+    m.close()
+    names = {O.ISA_SCALAR: "scalar", O.ISA_AVX2: "avx2", O.ISA_AVX512: "avx512"}
+    return {"value": n / sec, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"reference qm_model_forward ({names[isa]}, {threads} threads), {args.workload}: "
+                      f"{npre} prompt tokens then {n} greedy decode tokens timed"}
+
+
+def reference_arm(args, wl: dict) -> dict | None:
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+
+    threads = os.cpu_count() or 1
+    m, isa = ref_model(wl, args.workload, threads)
+    prompt = prompt_ids(wl)
+    lg = None
+    for p, t in enumerate(prompt):
+        lg = m.forward(int(t), p)
+    tok = int(np.argmax(lg))
+    pos = len(prompt)
+    for _ in range(args.warmup):
+        tok = int(np.argmax(m.forward(tok, pos)))
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = int(np.argmax(m.forward(tok, pos)))
+        pos += 1
+    sec = time.perf_counter() - t0
+    m.close()
+    names = {O.ISA_SCALAR: "scalar", O.ISA_AVX2: "avx2", O.ISA_AVX512: "avx512"}
+    v = args.steps / sec
+    c = wl["cfg"]
+    return {"metric": METRIC, "impl": "reference", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "i8xi8->i32, f32",
+            "data": f"synthetic: {wl['model']}; random prompt ids (numpy default_rng({wl['seed'] + 1000}))",
+            "config": {"workload": f"{args.workload}_decode", "model": wl["model"], "global_batch": 1,
+                       "seq_len": c["max_seq"], "prompt_tokens": len(prompt),
+                       "decode_positions": [len(prompt) + args.warmup, pos - 1], "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference",
+                             "sample": f"reference qm_model_forward ({names[isa]}, {threads} threads): "
+                                       f"{len(prompt)} prompt tokens untimed, {args.warmup} warm-up and "
+                                       f"{args.steps} timed greedy decode steps"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["quillm_b200", "reference"], default="quillm_b200")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="llama7b_q4_0")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="skip the matvec / prefill sweeps")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    wl = WORKLOADS[args.workload]
+    out = reference_arm(args, wl) if args.impl == "reference" else gpu_arm(args, wl)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

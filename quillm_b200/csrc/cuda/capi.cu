@@ -1,0 +1,265 @@
+// C-ABI entry points of libquillm_cuda (include/quillm_cuda.h): error state, per-device context and the
+// operator-level calls.  Model-level calls live in model.cu.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "gemv.cuh"
+#include "matmul.cuh"
+
+namespace qmc {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return set_error(e == cudaErrorMemoryAllocation ? QMC_ENOMEM : QMC_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+namespace {
+constexpr int kMaxDev = 64;
+DevCtx g_ctx[kMaxDev];
+std::mutex g_mu;
+}  // namespace
+
+DevCtx *ctx() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDev) {
+        set_error(QMC_ECUDA, "no CUDA device");
+        return nullptr;
+    }
+    DevCtx *c = &g_ctx[d];
+    if (c->device == d) return c;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (c->device == d) return c;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, d) != cudaSuccess) {
+        set_error(QMC_ECUDA, "cudaGetDeviceProperties failed");
+        return nullptr;
+    }
+    if (prop.major < 10) {
+        set_error(QMC_ECUDA, "device %d is sm_%d%d; libquillm_cuda is built for sm_100a", d, prop.major, prop.minor);
+        return nullptr;
+    }
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&c->err, sizeof(int)) != cudaSuccess || cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess) {
+        set_error(QMC_ECUDA, "device context setup failed");
+        return nullptr;
+    }
+    c->num_sms = prop.multiProcessorCount;
+    c->max_smem_optin = prop.sharedMemPerBlockOptin;
+    c->device = d;
+    return c;
+}
+
+// host (cos, sin) table row: same double expressions as src/ops.c:116-118, rounded to float
+void rope_row_host(int64_t pos, int64_t hd, float theta, float *out_cs) {
+    for (int64_t i = 0; i < hd / 2; i++) {
+        const double freq = pow((double)theta, -2.0 * (double)i / (double)hd);
+        const double ang = (double)pos * freq;
+        out_cs[2 * i] = (float)cos(ang);
+        out_cs[2 * i + 1] = (float)sin(ang);
+    }
+}
+
+// scratch that grows on demand (operator-level prefill only; models own their buffers)
+static int ensure_scratch(DevCtx *c, size_t bytes, void **out) {
+    static thread_local void *buf[kMaxDev];
+    static thread_local size_t cap[kMaxDev];
+    const int d = c->device;
+    if (cap[d] < bytes) {
+        if (buf[d]) {
+            cudaStreamSynchronize(c->stream);
+            cudaFree(buf[d]);
+            buf[d] = nullptr;
+            cap[d] = 0;
+        }
+        QMC_CUDA(cudaMalloc(&buf[d], bytes));
+        cap[d] = bytes;
+    }
+    *out = buf[d];
+    return QMC_OK;
+}
+
+}  // namespace qmc
+
+using namespace qmc;
+
+#define CTX_OR_FAIL()                                                                                                  \
+    DevCtx *c_ = ctx();                                                                                                \
+    if (!c_) return QMC_ECUDA;                                                                                         \
+    (void)c_
+
+extern "C" {
+
+const char *qmc_last_error(void) { return g_err; }
+
+int qmc_device_count(int *count) {
+    if (!count) return set_error(QMC_EINVAL, "null count");
+    QMC_CUDA(cudaGetDeviceCount(count));
+    return QMC_OK;
+}
+
+int qmc_set_device(int device) {
+    QMC_CUDA(cudaSetDevice(device));
+    return ctx() ? QMC_OK : QMC_ECUDA;
+}
+
+int qmc_get_device(int *device) {
+    QMC_CUDA(cudaGetDevice(device));
+    return QMC_OK;
+}
+
+int qmc_stream(void **stream) {
+    CTX_OR_FAIL();
+    *stream = (void *)c_->stream;
+    return QMC_OK;
+}
+
+int qmc_sync(void) {
+    CTX_OR_FAIL();
+    QMC_CUDA(cudaStreamSynchronize(c_->stream));
+    return qmc_check_device_error();
+}
+
+int qmc_check_device_error(void) {
+    CTX_OR_FAIL();
+    int v = 0;
+    QMC_CUDA(cudaMemcpy(&v, c_->err, sizeof v, cudaMemcpyDeviceToHost));
+    if (v) {
+        QMC_CUDA(cudaMemset(c_->err, 0, sizeof(int)));
+        return set_error(QMC_ETIMEOUT, "a device-side bounded wait expired (code %d)", v);
+    }
+    return QMC_OK;
+}
+
+int qmc_malloc(void **dptr, size_t bytes) {
+    CTX_OR_FAIL();
+    QMC_CUDA(cudaMalloc(dptr, bytes ? bytes : 1));
+    return QMC_OK;
+}
+int qmc_free(void *dptr) {
+    QMC_CUDA(cudaFree(dptr));
+    return QMC_OK;
+}
+int qmc_memcpy_h2d(void *dst, const void *src, size_t bytes, void *stream) {
+    CTX_OR_FAIL();
+    QMC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, pick_stream(stream)));
+    return QMC_OK;
+}
+int qmc_memcpy_d2h(void *dst, const void *src, size_t bytes, void *stream) {
+    CTX_OR_FAIL();
+    QMC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, pick_stream(stream)));
+    return QMC_OK;
+}
+int qmc_host_alloc(void **hptr, size_t bytes) {
+    QMC_CUDA(cudaMallocHost(hptr, bytes ? bytes : 1));
+    return QMC_OK;
+}
+int qmc_host_free(void *hptr) {
+    QMC_CUDA(cudaFreeHost(hptr));
+    return QMC_OK;
+}
+
+int qmc_quantize_rows(int dtype, const float *x, void *out, int64_t rows, int64_t cols, void *stream) {
+    CTX_OR_FAIL();
+    return launch_quantize_rows(dtype, x, out, rows, cols, pick_stream(stream));
+}
+
+int qmc_dequantize_rows(int dtype, const void *in, float *y, int64_t rows, int64_t cols, void *stream) {
+    CTX_OR_FAIL();
+    if (dtype != QMC_F32 && dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "bad dtype");
+    return launch_dequantize_rows(dtype, in, y, rows, cols, pick_stream(stream));
+}
+
+int qmc_matvec(int dtype, const void *W, int64_t rows, int64_t cols, const float *x, float *y, void *xq,
+               void *stream) {
+    CTX_OR_FAIL();
+    if (!W || !x || !y) return set_error(QMC_EINVAL, "matvec: null pointer");
+    if (rows <= 0 || cols <= 0) return QMC_OK;
+    GemvArgs a;
+    a.dtype = dtype;
+    a.W0 = W;
+    a.rows = rows;
+    a.K = cols;
+    a.x = x;
+    a.y = y;
+    a.epi = EPI_STORE;
+    a.xq_out = dtype == QMC_F32 ? nullptr : xq;
+    return launch_gemv(a, pick_stream(stream), false);
+}
+
+int qmc_matmul_nt(const float *A, const float *B, float *C, int64_t M, int64_t N, int64_t K, void *stream) {
+    CTX_OR_FAIL();
+    if (M <= 0 || N <= 0) return QMC_OK;
+    if (!A || !B || !C || K < 0) return set_error(QMC_EINVAL, "matmul_nt: bad arguments");
+    return launch_gemm_f32(A, B, C, M, N, K, pick_stream(stream));
+}
+
+int qmc_matmul_nt_q(int dtype, const void *W, const float *A, float *C, int64_t T, int64_t N, int64_t K,
+                    void *stream) {
+    CTX_OR_FAIL();
+    if (T <= 0 || N <= 0) return QMC_OK;
+    if (!W || !A || !C || K <= 0) return set_error(QMC_EINVAL, "matmul_nt_q: bad arguments");
+    if (dtype == QMC_F32) return launch_gemm_f32(A, (const float *)W, C, T, N, K, pick_stream(stream));
+    const int64_t nb = nblocks(K);
+    void *scr = nullptr;
+    const size_t qbytes = (size_t)(T * nb * 32 + 255) / 256 * 256;
+    int rc = ensure_scratch(c_, qbytes + (size_t)T * nb * 4, &scr);
+    if (rc) return rc;
+    int8_t *aq = (int8_t *)scr;
+    float *ad = (float *)((uint8_t *)scr + qbytes);
+    cudaStream_t s = pick_stream(stream);
+    if ((rc = launch_quantize_act(A, T, K, aq, ad, s))) return rc;
+    return launch_matmul_q(dtype, W, aq, ad, C, T, N, K, s);
+}
+
+int qmc_rmsnorm(float *out, const float *x, const float *w, int64_t n, float eps, void *stream) {
+    CTX_OR_FAIL();
+    if (n <= 0) return QMC_OK;
+    return launch_rmsnorm(out, x, w, n, eps, pick_stream(stream));
+}
+
+int qmc_softmax(float *x, int64_t n, void *stream) {
+    CTX_OR_FAIL();
+    return launch_softmax(x, n, pick_stream(stream));
+}
+
+int qmc_rope(float *v, int64_t n_heads, int64_t head_dim, int64_t pos, float theta, void *stream) {
+    CTX_OR_FAIL();
+    if (head_dim / 2 > kMaxRopeHalf) return set_error(QMC_EINVAL, "rope: head_dim > %d", 2 * kMaxRopeHalf);
+    RopeRow cs;
+    rope_row_host(pos, head_dim, theta, cs.v);
+    return launch_rope(v, n_heads, head_dim, cs, pick_stream(stream));
+}
+
+int qmc_swiglu(float *gate, const float *up, int64_t n, void *stream) {
+    CTX_OR_FAIL();
+    return launch_swiglu(gate, up, n, pick_stream(stream));
+}
+
+int qmc_argmax(const float *x, int32_t n, int32_t *out_index, void *stream) {
+    CTX_OR_FAIL();
+    if (n <= 0 || !x || !out_index) return set_error(QMC_EINVAL, "argmax: bad arguments");
+    return launch_argmax(x, n, out_index, pick_stream(stream), false);
+}
+
+int qmc_dot(int dtype, const void *w, const void *xq, int64_t n, float *out, void *stream) {
+    CTX_OR_FAIL();
+    if (dtype != QMC_F32 && dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "bad dtype");
+    return launch_dot(dtype, w, xq, n, out, pick_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,139 @@
+// Shared device helpers for libquillm_cuda (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "quillm_cuda.h"
+
+namespace qmc {
+
+constexpr int kQ8Bytes = 34;  // {fp16 d; int8 qs[32]}
+constexpr int kQ4Bytes = 18;  // {fp16 d; uint8 qs[16]}
+
+__host__ __device__ inline int64_t nblocks(int64_t n) { return (n + 31) / 32; }
+__host__ __device__ inline int64_t row_bytes(int dtype, int64_t n) {
+    return dtype == QMC_F32 ? n * 4 : nblocks(n) * (dtype == QMC_Q8_0 ? kQ8Bytes : kQ4Bytes);
+}
+
+// ---------------------------------------------------------------- fp16 bits
+// fp16 -> fp32 is exact (hardware cvt); fp32 -> fp16 is IEEE round-to-nearest-even (hardware cvt)
+// with the reference's NaN rule (quiet, top 10 payload bits kept: src/fp16.c:40-41).
+__device__ __forceinline__ float h2f(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
+__device__ __forceinline__ uint32_t f2h(float f) {
+    uint32_t b = __float_as_uint(f);
+    if ((b & 0x7fffffffu) > 0x7f800000u) return ((b >> 16) & 0x8000u) | 0x7e00u | ((b >> 13) & 0x3ffu);
+    return __half_as_ushort(__float2half_rn(f));
+}
+
+// ---------------------------------------------------------------- warp reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------- block quantization (warp per block)
+// Lane i holds element i of a 32-element block (0 for the zero-padded tail).  Every lane returns
+// its quantized value; *dd receives fp32(fp16(amax / qmax)) and *dh its fp16 bits.  Bit-exact with
+// src/quant.c:33-53: amax ignores NaN (the reference's `a > amax` test), IEEE division, rintf
+// (round half to even), clamp, q = 0 when the scale is 0.
+__device__ __forceinline__ int quant_lane(float v, float qmax, int qmin, int qmaxi, float *dd, uint32_t *dh) {
+    float a = fabsf(v);
+    uint32_t ab = (a == a) ? __float_as_uint(a) : 0u;  // |v| bits order like floats; NaN -> 0
+    uint32_t mb = __reduce_max_sync(0xffffffffu, ab);
+    float d = __fdiv_rn(__uint_as_float(mb), qmax);
+    uint32_t hb = f2h(d);
+    float sc = h2f(hb);
+    *dd = sc;
+    *dh = hb;
+    if (sc == 0.0f) return 0;
+    float r = rintf(__fdiv_rn(v, sc));
+    r = r < (float)qmin ? (float)qmin : r;
+    r = r > (float)qmaxi ? (float)qmaxi : r;
+    return (int)r;
+}
+
+// ---------------------------------------------------------------- error word
+// Kernels whose spin-waits expire OR a code into *err and return; the host reads it with
+// qmc_check_device_error().
+enum : int { kErrMbarTimeout = 1, kErrFlagTimeout = 2 };
+__device__ __forceinline__ void raise_error(int *err, int code) {
+    if (err) atomicOr(err, code);
+}
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+// ---------------------------------------------------------------- mbarrier + bulk async copy (1-D TMA)
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t *bar, uint32_t tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(tx) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// bounded wait: true when the phase completed, false after ~kWaitCycles
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
+// global -> shared bulk copy completing on `bar`; dst, src 16-byte aligned, bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+}  // namespace qmc
+
+// ---------------------------------------------------------------- host side (qmc_* internals)
+namespace qmc {
+int set_error(int code, const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);
+struct DevCtx {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    int *err = nullptr;  // device error word
+    int num_sms = 0;
+    size_t max_smem_optin = 0;
+};
+DevCtx *ctx();  // context of the calling thread's current device (created on first use); nullptr on failure
+inline cudaStream_t pick_stream(void *s) { return s ? (cudaStream_t)s : (ctx() ? ctx()->stream : nullptr); }
+}  // namespace qmc
+
+#define QMC_CUDA(call)                                                                                                 \
+    do {                                                                                                               \
+        cudaError_t e_ = (call);                                                                                       \
+        if (e_ != cudaSuccess) return qmc::cuda_fail(e_, #call);                                                       \
+    } while (0)
+#define QMC_LAUNCH_CHECK() QMC_CUDA(cudaGetLastError())

@@ -1,0 +1,538 @@
+// Whole-model decode on the device (src/model.c:158-191), one CUDA graph per model.
+//
+// HBM layout (per GPU; with tensor parallelism each rank holds its shard):
+//   wqkv  [Dl + 2*KVl rows][row_bytes(D)]   wq, wk, wv row shards stacked (bytes unchanged from the file)
+//   wo    [D rows][row_bytes(Dl)]            K-shard (this rank's heads' input columns)
+//   w1,w3 [Hl rows][row_bytes(D)], w2 [D rows][row_bytes(Hl)] (K-shard), output [Vl rows][row_bytes(D)]
+//   tok_embd full, norms full (f32)
+//   K/V caches f32 [L][max_seq][KVl], RoPE table f32x2 [max_seq][hd/2]
+// Step (graph): embed -> L x { qkv GEMV (rmsnorm+quant prologue, RoPE + cache-store epilogue),
+//   attention, wo GEMV (+residual), [all-reduce], w1/w3 GEMV (rmsnorm prologue, SwiGLU epilogue),
+//   w2 GEMV (+residual), [all-reduce] } -> output GEMV (final rmsnorm) [all-gather] -> argmax/advance.
+// Every kernel is launched with programmatic dependent launch so a GEMV's weight prefetch starts while
+// the previous kernel drains.  Residual + all-reduce: rank 0 adds its partial product into x, other
+// ranks store theirs, then one in-place sum all-reduce of D floats gives x + sum of partials everywhere.
+#include <nccl.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <vector>
+
+#include "attention.cuh"
+#include "elementwise.cuh"
+#include "gemv.cuh"
+#include "synth.cuh"
+
+using namespace qmc;
+
+namespace {
+struct Layer {
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+    uint8_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w3 = nullptr, *w2 = nullptr;
+    int dt[12];  // dtype per uploaded kind (indices QMC_T_*), -1 = missing
+};
+}  // namespace
+
+struct qmc_model {
+    qmc_config cfg;
+    int dev = 0, rank = 0, tp = 1;
+    ncclComm_t comm = nullptr;
+    cudaStream_t stream = nullptr;
+    int D, H, L, NH, NKV, V, S, hd, KVD;  // full model
+    int NHl, NKVl, Dl, KVl, Hl, Vl;       // this rank
+    int dt_tok = -1, dt_out = -1;
+    uint8_t *tok = nullptr, *out = nullptr;
+    float *norm = nullptr;
+    std::vector<Layer> layers;
+    std::vector<void *> allocs;
+    float *x = nullptr, *xb = nullptr, *q = nullptr, *h = nullptr, *logits_l = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr, *attn_part = nullptr;
+    float2 *rope = nullptr;
+    int *state = nullptr;  // [0] token  [1] pos  [2] step  [3] prompt length
+    int *forced = nullptr, *gen = nullptr, *attn_cnt = nullptr;
+    int *h_state = nullptr;
+    float *h_logits = nullptr;
+    AttnPlan ap;
+    cudaGraphExec_t graph = nullptr;
+    bool have_tok = false, have_norm = false, have_out = false;
+};
+
+namespace {
+
+int64_t rbytes(int dt, int64_t cols) { return row_bytes(dt, cols); }
+
+int dalloc(qmc_model *m, void **p, size_t bytes) {
+    cudaError_t e = cudaMalloc(p, bytes + 256);  // slack: 16-byte line reads past a tensor's end stay inside
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(model)");
+    m->allocs.push_back(*p);
+    return QMC_OK;
+}
+
+bool valid_dt(int dt) { return dt == QMC_F32 || dt == QMC_Q8_0 || dt == QMC_Q4_0; }
+
+// shard plan of one tensor kind on this rank: rows [r0, r0+nr) and columns [c0, c0+nc) of the full
+// tensor, plus the destination and the row offset inside a stacked buffer
+struct Shard {
+    int64_t rows, cols, r0, nr, c0, nc;
+};
+
+Shard shard_of(const qmc_model *m, int kind) {
+    const int64_t D = m->D, H = m->H, KV = m->KVD, V = m->V;
+    Shard s{};
+    auto rowsplit = [&](int64_t R, int64_t C, int64_t Rl) { s = Shard{R, C, m->rank * Rl, Rl, 0, C}; };
+    auto colsplit = [&](int64_t R, int64_t C, int64_t Cl) { s = Shard{R, C, 0, R, m->rank * Cl, Cl}; };
+    switch (kind) {
+    case QMC_T_TOK_EMBD: s = Shard{V, D, 0, V, 0, D}; break;
+    case QMC_T_NORM: case QMC_T_ATTN_NORM: case QMC_T_FFN_NORM: s = Shard{D, 0, 0, D, 0, 0}; break;
+    case QMC_T_OUTPUT: rowsplit(V, D, m->Vl); break;
+    case QMC_T_WQ: rowsplit(D, D, m->Dl); break;
+    case QMC_T_WK: case QMC_T_WV: rowsplit(KV, D, m->KVl); break;
+    case QMC_T_WO: colsplit(D, D, m->Dl); break;
+    case QMC_T_W1: case QMC_T_W3: rowsplit(H, D, m->Hl); break;
+    case QMC_T_W2: colsplit(D, H, m->Hl); break;
+    }
+    return s;
+}
+
+// destination buffer for (kind, layer, dtype), allocating it on first use
+int dest_of(qmc_model *m, int kind, int layer, int dt, uint8_t **dst) {
+    Layer *Ly = (layer >= 0 && layer < m->L) ? &m->layers[layer] : nullptr;
+    const Shard s = shard_of(m, kind);
+    int rc = QMC_OK;
+    auto need = [&](uint8_t **buf, size_t bytes) -> int {
+        if (!*buf) rc = dalloc(m, (void **)buf, bytes);
+        return rc;
+    };
+    switch (kind) {
+    case QMC_T_TOK_EMBD:
+        if (m->tok && m->dt_tok != dt) return set_error(QMC_EINVAL, "tok_embd dtype changed");
+        m->dt_tok = dt;
+        if (need(&m->tok, (size_t)(s.nr * rbytes(dt, s.nc)))) return rc;
+        *dst = m->tok;
+        return QMC_OK;
+    case QMC_T_OUTPUT:
+        if (m->out && m->dt_out != dt) return set_error(QMC_EINVAL, "output dtype changed");
+        m->dt_out = dt;
+        if (need(&m->out, (size_t)(s.nr * rbytes(dt, s.nc)))) return rc;
+        *dst = m->out;
+        return QMC_OK;
+    case QMC_T_NORM:
+        if (need((uint8_t **)&m->norm, (size_t)m->D * 4)) return rc;
+        *dst = (uint8_t *)m->norm;
+        return QMC_OK;
+    default: break;
+    }
+    if (!Ly) return set_error(QMC_EINVAL, "layer %d out of range", layer);
+    // grouped tensors must share a dtype (they are streamed by one kernel)
+    auto group_dt = [&](std::initializer_list<int> kinds) -> int {
+        for (int k : kinds)
+            if (Ly->dt[k] >= 0 && Ly->dt[k] != dt) return set_error(QMC_EINVAL, "layer %d: mixed dtypes in a fused group", layer);
+        return QMC_OK;
+    };
+    switch (kind) {
+    case QMC_T_ATTN_NORM:
+        if (need((uint8_t **)&Ly->attn_norm, (size_t)m->D * 4)) return rc;
+        *dst = (uint8_t *)Ly->attn_norm;
+        return QMC_OK;
+    case QMC_T_FFN_NORM:
+        if (need((uint8_t **)&Ly->ffn_norm, (size_t)m->D * 4)) return rc;
+        *dst = (uint8_t *)Ly->ffn_norm;
+        return QMC_OK;
+    case QMC_T_WQ: case QMC_T_WK: case QMC_T_WV: {
+        if ((rc = group_dt({QMC_T_WQ, QMC_T_WK, QMC_T_WV}))) return rc;
+        const int64_t rb = rbytes(dt, m->D);
+        if (need(&Ly->wqkv, (size_t)((m->Dl + 2 * m->KVl) * rb))) return rc;
+        const int64_t off = kind == QMC_T_WQ ? 0 : (kind == QMC_T_WK ? m->Dl : m->Dl + m->KVl);
+        *dst = Ly->wqkv + off * rb;
+        return QMC_OK;
+    }
+    case QMC_T_WO:
+        if (need(&Ly->wo, (size_t)(m->D * rbytes(dt, m->Dl)))) return rc;
+        *dst = Ly->wo;
+        return QMC_OK;
+    case QMC_T_W1: case QMC_T_W3:
+        if ((rc = group_dt({QMC_T_W1, QMC_T_W3}))) return rc;
+        if (need(kind == QMC_T_W1 ? &Ly->w1 : &Ly->w3, (size_t)(m->Hl * rbytes(dt, m->D)))) return rc;
+        *dst = kind == QMC_T_W1 ? Ly->w1 : Ly->w3;
+        return QMC_OK;
+    case QMC_T_W2:
+        if (need(&Ly->w2, (size_t)(m->D * rbytes(dt, m->Hl)))) return rc;
+        *dst = Ly->w2;
+        return QMC_OK;
+    }
+    return set_error(QMC_EINVAL, "unknown tensor kind %d", kind);
+}
+
+void mark(qmc_model *m, int kind, int layer, int dt) {
+    if (kind == QMC_T_TOK_EMBD) m->have_tok = true;
+    else if (kind == QMC_T_NORM) m->have_norm = true;
+    else if (kind == QMC_T_OUTPUT) m->have_out = true;
+    else m->layers[layer].dt[kind] = dt;
+}
+
+bool complete(const qmc_model *m) {
+    if (!m->have_tok || !m->have_norm || !m->have_out) return false;
+    for (const Layer &l : m->layers)
+        for (int k = QMC_T_ATTN_NORM; k <= QMC_T_W3; k++)
+            if (l.dt[k] < 0) return false;
+    return true;
+}
+
+#define RC(x)                                                                                                          \
+    do {                                                                                                               \
+        int rc_ = (x);                                                                                                 \
+        if (rc_) return rc_;                                                                                           \
+    } while (0)
+
+int nccl_check(ncclResult_t r, const char *what) {
+    if (r == ncclSuccess) return QMC_OK;
+    return set_error(QMC_ENCCL, "%s: %s", what, ncclGetErrorString(r));
+}
+
+// enqueue one decode step on m->stream (captured into the graph)
+int enqueue_step(qmc_model *m) {
+    cudaStream_t s = m->stream;
+    DevCtx *c = ctx();
+    const int *pos = m->state + 1;
+    RC(launch_embed(m->dt_tok, m->tok, m->D, m->state, m->x, s, true));
+    const int64_t kvstride = (int64_t)m->S * m->KVl;
+    for (int l = 0; l < m->L; l++) {
+        Layer &Ly = m->layers[l];
+        float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
+        GemvArgs a;
+        a.dtype = Ly.dt[QMC_T_WQ];
+        a.W0 = Ly.wqkv;
+        a.rows = m->Dl + 2 * m->KVl;
+        a.K = m->D;
+        a.x = m->x;
+        a.norm_w = Ly.attn_norm;
+        a.eps = m->cfg.norm_eps;
+        a.epi = EPI_QKV;
+        a.q = m->q;
+        a.kcache = kcl;
+        a.vcache = vcl;
+        a.Dq = m->Dl;
+        a.KVl = m->KVl;
+        a.hd = m->hd;
+        a.rope = m->rope;
+        a.pos = pos;
+        a.err = c->err;
+        RC(launch_gemv(a, s, true));
+        RC(launch_attention(m->ap, m->q, kcl, vcl, m->xb, m->attn_part, m->attn_cnt, pos, m->NKVl, m->NH / m->NKV,
+                            m->hd, m->KVl, s, true));
+        GemvArgs o;
+        o.dtype = Ly.dt[QMC_T_WO];
+        o.W0 = Ly.wo;
+        o.rows = m->D;
+        o.K = m->Dl;
+        o.x = m->xb;
+        o.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
+        o.y = m->x;
+        o.err = c->err;
+        RC(launch_gemv(o, s, true));
+        if (m->tp > 1) RC(nccl_check(ncclAllReduce(m->x, m->x, m->D, ncclFloat, ncclSum, m->comm, s), "all-reduce(wo)"));
+        GemvArgs f;
+        f.dtype = Ly.dt[QMC_T_W1];
+        f.W0 = Ly.w1;
+        f.W1 = Ly.w3;
+        f.rows = m->Hl;
+        f.K = m->D;
+        f.x = m->x;
+        f.norm_w = Ly.ffn_norm;
+        f.eps = m->cfg.norm_eps;
+        f.epi = EPI_SWIGLU;
+        f.y = m->h;
+        f.err = c->err;
+        RC(launch_gemv(f, s, true));
+        GemvArgs d;
+        d.dtype = Ly.dt[QMC_T_W2];
+        d.W0 = Ly.w2;
+        d.rows = m->D;
+        d.K = m->Hl;
+        d.x = m->h;
+        d.epi = m->rank == 0 ? EPI_ADD : EPI_STORE;
+        d.y = m->x;
+        d.err = c->err;
+        RC(launch_gemv(d, s, true));
+        if (m->tp > 1) RC(nccl_check(ncclAllReduce(m->x, m->x, m->D, ncclFloat, ncclSum, m->comm, s), "all-reduce(w2)"));
+    }
+    GemvArgs g;
+    g.dtype = m->dt_out;
+    g.W0 = m->out;
+    g.rows = m->Vl;
+    g.K = m->D;
+    g.x = m->x;
+    g.norm_w = m->norm;
+    g.eps = m->cfg.norm_eps;
+    g.epi = EPI_STORE;
+    g.y = m->logits_l;
+    g.err = c->err;
+    RC(launch_gemv(g, s, true));
+    if (m->tp > 1)
+        RC(nccl_check(ncclAllGather(m->logits_l, m->logits, m->Vl, ncclFloat, m->comm, s), "all-gather(logits)"));
+    RC(launch_argmax(m->logits, m->V, m->state, s, true, m->state + 1, m->forced, m->state + 3, m->state + 2, m->gen,
+                     m->S));
+    return QMC_OK;
+}
+
+int build_graph(qmc_model *m) {
+    if (m->graph) return QMC_OK;
+    if (!complete(m)) return set_error(QMC_ESTATE, "model: not every tensor has been uploaded");
+    cudaGraph_t g = nullptr;
+    QMC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    return QMC_OK;
+}
+
+int check_dev(const qmc_model *m) {
+    int d = -1;
+    QMC_CUDA(cudaGetDevice(&d));
+    if (d != m->dev) QMC_CUDA(cudaSetDevice(m->dev));
+    return QMC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qmc_nccl_unique_id(void *id128) {
+    ncclUniqueId id;
+    RC(nccl_check(ncclGetUniqueId(&id), "ncclGetUniqueId"));
+    memcpy(id128, &id, sizeof id);
+    return QMC_OK;
+}
+
+int qmc_model_create(const qmc_config *cfg, int tp_rank, int tp_size, const void *nccl_id, qmc_model **out) {
+    if (!cfg || !out) return set_error(QMC_EINVAL, "model_create: null argument");
+    *out = nullptr;
+    DevCtx *c = ctx();
+    if (!c) return QMC_ECUDA;
+    const qmc_config &k = *cfg;
+    if (k.dim <= 0 || k.hidden_dim <= 0 || k.n_layers <= 0 || k.n_heads <= 0 || k.n_kv_heads <= 0 || k.vocab_size <= 0 ||
+        k.max_seq <= 0 || k.dim % k.n_heads || k.n_heads % k.n_kv_heads || (k.dim / k.n_heads) % 2)
+        return set_error(QMC_EINVAL, "model_create: inconsistent configuration");
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size) return set_error(QMC_EINVAL, "model_create: bad tp rank/size");
+    const int hd = k.dim / k.n_heads;
+    if (hd / 2 > kMaxRopeHalf) return set_error(QMC_EINVAL, "model_create: head_dim > 256");
+    if (tp_size > 1 && (k.n_kv_heads % tp_size || k.vocab_size % tp_size || (k.dim / tp_size) % 32 ||
+                        k.hidden_dim % (32 * tp_size)))
+        return set_error(QMC_EINVAL, "model_create: shapes do not shard %d ways on 32-element block boundaries", tp_size);
+    qmc_model *m = new qmc_model();
+    m->cfg = k;
+    m->rank = tp_rank;
+    m->tp = tp_size;
+    cudaGetDevice(&m->dev);
+    m->stream = c->stream;
+    m->D = k.dim, m->H = k.hidden_dim, m->L = k.n_layers, m->NH = k.n_heads, m->NKV = k.n_kv_heads;
+    m->V = k.vocab_size, m->S = k.max_seq, m->hd = hd, m->KVD = hd * k.n_kv_heads;
+    m->NHl = m->NH / tp_size, m->NKVl = m->NKV / tp_size, m->Dl = m->NHl * hd, m->KVl = m->NKVl * hd;
+    m->Hl = m->H / tp_size, m->Vl = m->V / tp_size;
+    m->layers.resize(m->L);
+    for (Layer &l : m->layers)
+        for (int i = 0; i < 12; i++) l.dt[i] = -1;
+    int rc = QMC_OK;
+    auto fail = [&](int r) {
+        qmc_model_free(m);
+        return r;
+    };
+    if (tp_size > 1) {
+        if (!nccl_id) return fail(set_error(QMC_EINVAL, "model_create: tp_size > 1 needs an NCCL id"));
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof id);
+        if ((rc = nccl_check(ncclCommInitRank(&m->comm, tp_size, id, tp_rank), "ncclCommInitRank"))) return fail(rc);
+    }
+    m->ap = plan_attention(m->NKVl, m->NH / m->NKV, hd, m->S, c->num_sms);
+    const size_t kvbytes = (size_t)m->L * m->S * m->KVl * 4;
+    if ((rc = dalloc(m, (void **)&m->x, (size_t)m->D * 4)) || (rc = dalloc(m, (void **)&m->xb, (size_t)m->Dl * 4)) ||
+        (rc = dalloc(m, (void **)&m->q, (size_t)m->Dl * 4)) || (rc = dalloc(m, (void **)&m->h, (size_t)m->Hl * 4)) ||
+        (rc = dalloc(m, (void **)&m->logits, (size_t)m->V * 4)) || (rc = dalloc(m, (void **)&m->kc, kvbytes)) ||
+        (rc = dalloc(m, (void **)&m->vc, kvbytes)) || (rc = dalloc(m, (void **)&m->attn_part, m->ap.part_floats * 4)) ||
+        (rc = dalloc(m, (void **)&m->attn_cnt, (size_t)m->NKVl * 4)) ||
+        (rc = dalloc(m, (void **)&m->rope, (size_t)m->S * (hd / 2) * 8)) || (rc = dalloc(m, (void **)&m->state, 16)) ||
+        (rc = dalloc(m, (void **)&m->forced, (size_t)m->S * 4)) || (rc = dalloc(m, (void **)&m->gen, (size_t)m->S * 4)))
+        return fail(rc);
+    m->logits_l = tp_size > 1 ? nullptr : m->logits;
+    if (tp_size > 1 && (rc = dalloc(m, (void **)&m->logits_l, (size_t)m->Vl * 4))) return fail(rc);
+    if (cudaMallocHost(&m->h_state, 64) != cudaSuccess || cudaMallocHost(&m->h_logits, (size_t)m->V * 4) != cudaSuccess)
+        return fail(set_error(QMC_ENOMEM, "pinned host buffers"));
+    // zeroed caches/counters, RoPE table from the reference's double expressions
+    if (cudaMemsetAsync(m->kc, 0, kvbytes, m->stream) || cudaMemsetAsync(m->vc, 0, kvbytes, m->stream) ||
+        cudaMemsetAsync(m->attn_cnt, 0, (size_t)m->NKVl * 4, m->stream) || cudaMemsetAsync(m->state, 0, 16, m->stream))
+        return fail(set_error(QMC_ECUDA, "memset"));
+    std::vector<float> tab((size_t)m->S * hd);
+    for (int p = 0; p < m->S; p++) rope_row_host(p, hd, k.rope_theta, tab.data() + (size_t)p * hd);
+    if (cudaMemcpy(m->rope, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return fail(set_error(QMC_ECUDA, "rope table upload"));
+    *out = m;
+    return QMC_OK;
+}
+
+int qmc_model_upload(qmc_model *m, int kind, int layer, int dtype, int64_t rows, int64_t cols, const void *host) {
+    if (!m || !host) return set_error(QMC_EINVAL, "upload: null argument");
+    RC(check_dev(m));
+    if (kind < 0 || kind > QMC_T_W3) return set_error(QMC_EINVAL, "upload: bad kind");
+    if (!valid_dt(dtype)) return set_error(QMC_EINVAL, "upload: bad dtype %d", dtype);
+    const bool vec = kind == QMC_T_NORM || kind == QMC_T_ATTN_NORM || kind == QMC_T_FFN_NORM;
+    const Shard s = shard_of(m, kind);
+    if (vec ? (dtype != QMC_F32 || rows != s.rows || cols != 0) : (rows != s.rows || cols != s.cols))
+        return set_error(QMC_EINVAL, "upload: kind %d layer %d has shape %lldx%lld, expected %lldx%lld", kind, layer,
+                         (long long)rows, (long long)cols, (long long)s.rows, (long long)s.cols);
+    uint8_t *dst = nullptr;
+    RC(dest_of(m, kind, layer, dtype, &dst));
+    const uint8_t *src = (const uint8_t *)host;
+    if (vec) {
+        QMC_CUDA(cudaMemcpy(dst, src, (size_t)rows * 4, cudaMemcpyHostToDevice));
+    } else if (s.c0 == 0 && s.nc == s.cols) {  // row shard: contiguous
+        const int64_t rb = rbytes(dtype, cols);
+        QMC_CUDA(cudaMemcpy(dst, src + s.r0 * rb, (size_t)(s.nr * rb), cudaMemcpyHostToDevice));
+    } else {  // column shard: strided gather of each row's block range
+        const int64_t rb = rbytes(dtype, cols), rbl = rbytes(dtype, s.nc), off = rbytes(dtype, s.c0);
+        QMC_CUDA(cudaMemcpy2D(dst, (size_t)rbl, src + off, (size_t)rb, (size_t)rbl, (size_t)s.nr, cudaMemcpyHostToDevice));
+    }
+    mark(m, kind, layer, dtype);
+    if (m->graph) {  // a re-upload keeps the graph valid (same buffers)
+    }
+    return QMC_OK;
+}
+
+int qmc_model_synthesize(qmc_model *m, int dtype, uint64_t seed, double stdv) {
+    if (!m) return set_error(QMC_EINVAL, "synthesize: null model");
+    RC(check_dev(m));
+    if (!valid_dt(dtype)) return set_error(QMC_EINVAL, "synthesize: bad dtype");
+    const int L = m->L;
+    for (int t = 0; t < 3 + 9 * L; t++) {
+        int kind, layer = -1;
+        if (t == 0) kind = QMC_T_TOK_EMBD;
+        else if (t == 1 + 9 * L) kind = QMC_T_NORM;
+        else if (t == 2 + 9 * L) kind = QMC_T_OUTPUT;
+        else {
+            static const int order[9] = {QMC_T_ATTN_NORM, QMC_T_WQ, QMC_T_WK, QMC_T_WV, QMC_T_WO,
+                                         QMC_T_FFN_NORM,  QMC_T_W1, QMC_T_W2, QMC_T_W3};
+            layer = (t - 1) / 9;
+            kind = order[(t - 1) % 9];
+        }
+        const bool vec = kind == QMC_T_NORM || kind == QMC_T_ATTN_NORM || kind == QMC_T_FFN_NORM;
+        const int dt = vec ? QMC_F32 : dtype;
+        uint8_t *dst = nullptr;
+        RC(dest_of(m, kind, layer, dt, &dst));
+        const Shard s = shard_of(m, kind);
+        if (vec) RC(launch_fill((float *)dst, m->D, 1.0f, m->stream));
+        else RC(launch_synth(seed, (uint64_t)t, dt, s.cols, s.r0, s.nr, s.c0, s.nc, stdv, dst, m->stream));
+        mark(m, kind, layer, dt);
+    }
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    return QMC_OK;
+}
+
+int qmc_model_forward(qmc_model *m, int32_t token, int32_t pos, float *logits_host, int32_t *next_token) {
+    if (!m) return set_error(QMC_EINVAL, "forward: null model");
+    if (token < 0 || token >= m->V || pos < 0 || pos >= m->S)
+        return set_error(QMC_EINVAL, "forward: token %d / pos %d out of range", token, pos);
+    RC(check_dev(m));
+    RC(build_graph(m));
+    m->h_state[0] = token, m->h_state[1] = pos, m->h_state[2] = 0, m->h_state[3] = 0;
+    QMC_CUDA(cudaMemcpyAsync(m->state, m->h_state, 16, cudaMemcpyHostToDevice, m->stream));
+    QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
+    if (logits_host) QMC_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, m->stream));
+    QMC_CUDA(cudaMemcpyAsync(m->h_state + 4, m->state, 4, cudaMemcpyDeviceToHost, m->stream));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    RC(qmc_check_device_error());
+    if (logits_host) memcpy(logits_host, m->h_logits, (size_t)m->V * 4);
+    if (next_token) *next_token = m->h_state[4];
+    return QMC_OK;
+}
+
+int qmc_model_generate(qmc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen, int32_t *out_tokens) {
+    if (!m || !prompt || n_prompt < 1 || n_gen < 0 || (n_gen && !out_tokens))
+        return set_error(QMC_EINVAL, "generate: bad arguments");
+    if (n_prompt + n_gen - 1 > m->S) return set_error(QMC_EINVAL, "generate: %d positions exceed max_seq %d", n_prompt + n_gen - 1, m->S);
+    for (int i = 0; i < n_prompt; i++)
+        if (prompt[i] < 0 || prompt[i] >= m->V) return set_error(QMC_EINVAL, "generate: prompt token out of range");
+    if (n_gen == 0) return QMC_OK;
+    RC(check_dev(m));
+    RC(build_graph(m));
+    QMC_CUDA(cudaMemcpyAsync(m->forced, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    m->h_state[0] = prompt[0], m->h_state[1] = 0, m->h_state[2] = 0, m->h_state[3] = n_prompt;
+    QMC_CUDA(cudaMemcpyAsync(m->state, m->h_state, 16, cudaMemcpyHostToDevice, m->stream));
+    const int steps = n_prompt + n_gen - 1;
+    for (int i = 0; i < steps; i++) QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
+    QMC_CUDA(cudaMemcpyAsync(out_tokens, m->gen, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, m->stream));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    return qmc_check_device_error();
+}
+
+int qmc_model_enqueue_decode(qmc_model *m, int32_t token, int32_t pos, int32_t steps) {
+    if (!m || token >= m->V || steps < 0 || (token >= 0 && (pos < 0 || pos + steps > m->S)))
+        return set_error(QMC_EINVAL, "enqueue_decode: bad arguments");
+    RC(check_dev(m));
+    RC(build_graph(m));
+    if (token >= 0) {  // token < 0: continue from the device's current (token, pos)
+        m->h_state[8] = token, m->h_state[9] = pos, m->h_state[10] = 0, m->h_state[11] = 1;
+        QMC_CUDA(cudaMemcpyAsync(m->forced, m->h_state + 8, 4, cudaMemcpyHostToDevice, m->stream));
+        QMC_CUDA(cudaMemcpyAsync(m->state, m->h_state + 8, 16, cudaMemcpyHostToDevice, m->stream));
+    }
+    for (int i = 0; i < steps; i++) QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
+    return QMC_OK;
+}
+
+int qmc_model_state(qmc_model *m, int32_t *token, int32_t *pos) {
+    if (!m) return set_error(QMC_EINVAL, "state: null model");
+    RC(check_dev(m));
+    QMC_CUDA(cudaMemcpyAsync(m->h_state + 12, m->state, 8, cudaMemcpyDeviceToHost, m->stream));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    if (token) *token = m->h_state[12];
+    if (pos) *pos = m->h_state[13];
+    return qmc_check_device_error();
+}
+
+int qmc_model_logits(qmc_model *m, const float **dev_logits) {
+    if (!m || !dev_logits) return set_error(QMC_EINVAL, "logits: null argument");
+    *dev_logits = m->logits;
+    return QMC_OK;
+}
+
+int qmc_model_config(const qmc_model *m, qmc_config *cfg) {
+    if (!m || !cfg) return set_error(QMC_EINVAL, "config: null argument");
+    *cfg = m->cfg;
+    return QMC_OK;
+}
+
+int qmc_model_step_bytes(const qmc_model *m, int32_t pos, double *bytes) {
+    if (!m || !bytes) return set_error(QMC_EINVAL, "step_bytes: null argument");
+    if (!complete(m)) return set_error(QMC_ESTATE, "step_bytes: model incomplete");
+    double b = 0.0;
+    for (const Layer &l : m->layers) {
+        b += (double)(m->Dl + 2 * m->KVl) * rbytes(l.dt[QMC_T_WQ], m->D);
+        b += (double)m->D * rbytes(l.dt[QMC_T_WO], m->Dl);
+        b += 2.0 * m->Hl * rbytes(l.dt[QMC_T_W1], m->D);
+        b += (double)m->D * rbytes(l.dt[QMC_T_W2], m->Hl);
+        b += 2.0 * (pos + 1) * m->KVl * 4.0;  // K and V reads
+    }
+    b += (double)m->Vl * rbytes(m->dt_out, m->D);
+    *bytes = b;
+    return QMC_OK;
+}
+
+int qmc_model_free(qmc_model *m) {
+    if (!m) return QMC_OK;
+    cudaSetDevice(m->dev);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->h_state) cudaFreeHost(m->h_state);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->comm) ncclCommDestroy(m->comm);
+    delete m;
+    return QMC_OK;
+}
+
+}  // extern "C"
