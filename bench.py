@@ -150,38 +150,62 @@ def cuda_events(stream_ptr: int):
     return st, torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def time_matvec(qb, torch, dt: int, rows: int, cols: int, iters: int = 60) -> tuple[float, float]:
-    """(seconds per launch, algorithmic bytes) of qmc_matvec, weights rotated over > 2x L2 of copies"""
+def _graph_time(torch, launch, n: int) -> float:
+    """seconds per launch of `launch(stream_ptr)` replayed n times from one captured CUDA graph (no host
+    launch overhead in the timing), CUDA events on the capture stream"""
+    st = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            launch(st.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(n):
+            launch(st.cuda_stream, i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / 1e3 / n
+
+
+def matvec_operands(torch, dt: int, rows: int, cols: int):
+    """rotating weight copies (> 2x L2 in total, so every launch streams from HBM) with valid fp16 scales"""
     rb = row_bytes(dt, cols)
     wbytes = rows * rb
-    algo = wbytes + 4 * cols + 34 * ((cols + 31) // 32) + 4 * rows
     copies = max(2, -(-256 * 2**20 // wbytes))
     g = torch.Generator(device="cuda").manual_seed(rows * 7 + cols)
     Ws = [torch.randint(0, 256, (wbytes + 256,), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
-    # valid scales: write fp16 0.01 into every block's d so the arithmetic stays finite
-    for w in Ws:
+    for w in Ws:  # fp16 0.01 as every block's scale keeps the arithmetic finite
         v = w[:wbytes].view(rows, -1, 34 if dt == Q8_0 else 18)
         v[:, :, 0] = 0x1F
         v[:, :, 1] = 0x21
     x = torch.randn(cols, device="cuda")
     y = torch.empty(rows, device="cuda")
     xq = torch.empty(34 * ((cols + 31) // 32), dtype=torch.uint8, device="cuda")
-    torch.cuda.synchronize()  # torch filled the inputs on its own stream
-    s = C.c_void_p()
-    qb.check(qb.cuda().qmc_stream(C.byref(s)))
-    st, e0, e1 = cuda_events(s.value)
-    for i in range(5):
-        qb.check(qb.cuda().qmc_matvec(dt, Ws[i % copies].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(),
-                                      xq.data_ptr(), None))
-    qb.check(qb.cuda().qmc_sync())
-    e0.record(st)
-    for i in range(iters):
-        qb.cuda().qmc_matvec(dt, Ws[i % copies].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(), xq.data_ptr(), None)
-    e1.record(st)
-    qb.check(qb.cuda().qmc_sync())
-    sec = e0.elapsed_time(e1) / 1e3 / iters
+    torch.cuda.synchronize()
+    algo = wbytes + 4 * cols + 34 * ((cols + 31) // 32) + 4 * rows
+    return Ws, x, y, xq, float(algo)
+
+
+def time_matvec(qb, torch, dt: int, rows: int, cols: int, iters: int = 64) -> tuple[float, float]:
+    """(seconds per launch, algorithmic bytes) of qmc_matvec"""
+    Ws, x, y, xq, algo = matvec_operands(torch, dt, rows, cols)
+    lib = qb.cuda()
+
+    def launch(stream, i=0):
+        qb.check(lib.qmc_matvec(dt, Ws[i % len(Ws)].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(),
+                                xq.data_ptr(), stream))
+
+    sec = _graph_time(torch, launch, iters)
     del Ws
-    return sec, float(algo)
+    return sec, algo
 
 
 def time_prefill(qb, torch, T: int, N: int, K: int, iters: int = 10) -> float:
@@ -191,18 +215,31 @@ def time_prefill(qb, torch, T: int, N: int, K: int, iters: int = 10) -> float:
     v[:, :, 1] = 0x21
     A = torch.randn(T, K, device="cuda")
     Cm = torch.empty(T, N, device="cuda")
-    torch.cuda.synchronize()
-    s = C.c_void_p()
-    qb.check(qb.cuda().qmc_stream(C.byref(s)))
-    st, e0, e1 = cuda_events(s.value)
-    qb.check(qb.cuda().qmc_matmul_nt_q(Q8_0, W.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, None))
+    lib = qb.cuda()
+
+    def launch(stream, i=0):
+        qb.check(lib.qmc_matmul_nt_q(Q8_0, W.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, stream))
+
+    return _graph_time(torch, launch, iters)
+
+
+def profile_matvec(spec: str) -> None:
+    """--profile-matvec ROWSxCOLS:DTYPE[:N]: N plain qmc_matvec launches (for ncu captures)"""
+    import torch
+
+    import quillm_b200 as qb
+
+    shape, dts, *rest = spec.split(":")
+    rows, cols = map(int, shape.split("x"))
+    dt = {"q8_0": Q8_0, "q4_0": Q4_0}[dts]
+    n = int(rest[0]) if rest else 4
+    qb.check(qb.cuda().qmc_set_device(0))
+    Ws, x, y, xq, _ = matvec_operands(torch, dt, rows, cols)
+    for i in range(n):
+        qb.check(qb.cuda().qmc_matvec(dt, Ws[i % len(Ws)].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(),
+                                      xq.data_ptr(), None))
     qb.check(qb.cuda().qmc_sync())
-    e0.record(st)
-    for _ in range(iters):
-        qb.cuda().qmc_matmul_nt_q(Q8_0, W.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, None)
-    e1.record(st)
-    qb.check(qb.cuda().qmc_sync())
-    return e0.elapsed_time(e1) / 1e3 / iters
+    print(f"profile-matvec {spec}: {n} launches ok")
 
 
 def traffic_from_profiles(tag: str):
@@ -456,10 +493,18 @@ def main():
     ap.add_argument("--workload", choices=list(WORKLOADS), default="llama7b_q4_0")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="skip the matvec / prefill sweeps")
+    ap.add_argument("--prompt", type=int, default=None, help="override the workload's prompt length")
+    ap.add_argument("--profile-matvec", default=None, metavar="ROWSxCOLS:DTYPE[:N]",
+                    help="only launch N plain matvecs (a small case for ncu captures)")
     args = ap.parse_args()
+    if args.profile_matvec:
+        profile_matvec(args.profile_matvec)
+        return
     if args.warmup < 3:
         args.warmup = 3
-    wl = WORKLOADS[args.workload]
+    wl = dict(WORKLOADS[args.workload])
+    if args.prompt is not None:
+        wl["prompt"] = max(1, args.prompt)
     out = reference_arm(args, wl) if args.impl == "reference" else gpu_arm(args, wl)
     if out is not None:
         print(json.dumps(out), flush=True)

@@ -1,182 +1,180 @@
 // Decode attention over the device-resident fp32 KV cache (src/model.c:132-156), split over positions.
 //
 // Batch-1 decode has only n_kv_heads (x group) heads, far fewer than the 148 SMs, so each KV head's
-// positions 0..pos are split into `nsplit` chunks, one CTA each (flash-decoding).  A CTA computes the
-// scores q.k * scale of all `group` query heads sharing its KV head (GQA: K/V read once), a local max
-// m, l = sum exp(s - m) and o = sum exp(s - m) v, and stores (m, l, o) to scratch.  The last CTA to
-// finish a KV head (atomic ticket) merges the splits: out = sum_j e^(m_j-M) o_j / sum_j e^(m_j-M) l_j.
-// Equal to the reference's softmax-then-weighted-sum up to float rounding.
+// positions 0..pos are split into `nsplit` chunks, one CTA each, and the nsplit CTAs of a head form one
+// thread-block cluster.  In a CTA every warp walks its positions once, reading K_t and V_t together
+// (coalesced, lanes across head_dim) with an online softmax per query head of the GQA group (K/V read
+// once for the whole group): running max m, l = sum e^(s-m), o = sum e^(s-m) v.  Warps merge in shared
+// memory; the cluster's rank-0 CTA then merges the nsplit partial (m, l, o) through distributed shared
+// memory and writes out = sum_j e^(m_j-M) o_j / sum_j e^(m_j-M) l_j.  Equal to the reference's
+// softmax-then-weighted-sum up to float rounding; no global scratch and no atomics.
+#include <cooperative_groups.h>
+
 #include "attention.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace qmc {
 namespace {
 
 constexpr int AT = 128;  // threads per CTA (4 warps)
-constexpr int MAXW = 8;  // head_dim / 32 upper bound (head_dim <= 256)
+constexpr int GMAX = 8;  // query heads per CTA (a larger GQA group spans several CTAs)
 
 struct AParams {
     const float *q, *kc, *vc;
-    float *out, *part;
-    int *cnt;
+    float *out;
     const int *pos;
-    int hd, group, kvl, nsplit, chunk_max;
+    int hd, group, gsplit, kvl, nsplit;
     float scale;
 };
 
+template <int MAXW>
 __global__ void __launch_bounds__(AT) attn_decode_kernel(const AParams p) {
     extern __shared__ __align__(16) float sm[];
-    const int g0 = blockIdx.x, split = blockIdx.y;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int kvh = blockIdx.x / p.gsplit, gs = blockIdx.x % p.gsplit, split = blockIdx.y;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int hd = p.hd, G = p.group, nw = (hd + 31) >> 5;
-    float *qs = sm;                               // [G][hd]
-    float *sc = qs + G * hd;                      // [G][chunk_max]
-    float *red = sc + G * p.chunk_max;            // [4][G][hd]
-    float *ml = red + 4 * G * hd;                 // [G][2]
+    const int hd = p.hd, h0 = gs * GMAX, G = min(GMAX, p.group - h0);
+    const int stride = hd + 2;
+    float *wpart = sm;                      // [4 warps][G][hd + 2]   per-warp (m, l, o)
+    float *cpart = sm + 4 * GMAX * stride;  // [G][hd + 2]            this CTA's merged (m, l, o)
     pdl_wait();
     const int npos = *p.pos + 1;
     const int chunk = (npos + p.nsplit - 1) / p.nsplit;
-    const int t0 = split * chunk;
-    const int t1 = min(npos, t0 + chunk);
-    const int n = max(0, t1 - t0);
-    const float *kbase = p.kc + (int64_t)g0 * hd, *vbase = p.vc + (int64_t)g0 * hd;
+    const int t0 = split * chunk, t1 = min(npos, t0 + chunk);
+    const int64_t hq = (int64_t)kvh * p.group + h0;  // first query head of this CTA
+    const float *kb = p.kc + (int64_t)kvh * hd, *vb = p.vc + (int64_t)kvh * hd;
 
-    for (int i = t; i < G * hd; i += AT) qs[i] = p.q[(int64_t)g0 * G * hd + i];
-    __syncthreads();
-
-    // scores: warp per position, lanes across head_dim
-    for (int j = warp; j < n; j += AT / 32) {
-        const float *kr = kbase + (int64_t)(t0 + j) * p.kvl;
-        float kv[MAXW];
+    float q[GMAX][MAXW], o[GMAX][MAXW], m[GMAX], l[GMAX];
 #pragma unroll
-        for (int m = 0; m < MAXW; m++) kv[m] = (m < nw && lane + 32 * m < hd) ? kr[lane + 32 * m] : 0.0f;
-        for (int g = 0; g < G; g++) {
-            float s = 0.0f;
+    for (int g = 0; g < GMAX; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.0f;
 #pragma unroll
-            for (int m = 0; m < MAXW; m++)
-                if (m < nw && lane + 32 * m < hd) s = fmaf(kv[m], qs[g * hd + lane + 32 * m], s);
-            s = warp_sum(s);
-            if (lane == 0) sc[g * p.chunk_max + j] = s * p.scale;
+        for (int w = 0; w < MAXW; w++) {
+            const int d = lane + 32 * w;
+            q[g][w] = (g < G && d < hd) ? p.q[(hq + g) * hd + d] : 0.0f;
+            o[g][w] = 0.0f;
         }
     }
-    __syncthreads();
-    // softmax statistics per head: warp g % 4
-    for (int g = warp; g < G; g += AT / 32) {
-        float mx = -INFINITY;
-        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[g * p.chunk_max + j]);
-        mx = warp_max(mx);
-        float l = 0.0f;
-        for (int j = lane; j < n; j += 32) {
-            const float e = n ? expf(sc[g * p.chunk_max + j] - mx) : 0.0f;
-            sc[g * p.chunk_max + j] = e;
-            l += e;
+    for (int tt = t0 + warp; tt < t1; tt += AT / 32) {
+        float k[MAXW], v[MAXW];
+#pragma unroll
+        for (int w = 0; w < MAXW; w++) {
+            const int d = lane + 32 * w;
+            k[w] = d < hd ? kb[(int64_t)tt * p.kvl + d] : 0.0f;
+            v[w] = d < hd ? vb[(int64_t)tt * p.kvl + d] : 0.0f;
         }
-        l = warp_sum(l);
-        if (lane == 0) ml[2 * g] = mx, ml[2 * g + 1] = l;
-    }
-    __syncthreads();
-    // o = sum_j e_j v_j: warp per position subset, lanes across head_dim
-    {
-        float acc[8][MAXW];
-        const int GG = G < 8 ? G : 8;
-        for (int g0b = 0; g0b < G; g0b += 8) {
 #pragma unroll
-            for (int g = 0; g < 8; g++)
+        for (int g = 0; g < GMAX; g++) {
+            if (g < G) {
+                float s = 0.0f;
 #pragma unroll
-                for (int m = 0; m < MAXW; m++) acc[g][m] = 0.0f;
-            for (int j = warp; j < n; j += AT / 32) {
-                const float *vr = vbase + (int64_t)(t0 + j) * p.kvl;
-                float vv[MAXW];
+                for (int w = 0; w < MAXW; w++) s = fmaf(k[w], q[g][w], s);
+                s = warp_sum(s) * p.scale;
+                const float mn = fmaxf(m[g], s);
+                const float corr = expf(m[g] - mn), e = expf(s - mn);
+                l[g] = l[g] * corr + e;
 #pragma unroll
-                for (int m = 0; m < MAXW; m++) vv[m] = (m < nw && lane + 32 * m < hd) ? vr[lane + 32 * m] : 0.0f;
-#pragma unroll
-                for (int g = 0; g < 8; g++)
-                    if (g0b + g < G) {
-                        const float e = sc[(g0b + g) * p.chunk_max + j];
-#pragma unroll
-                        for (int m = 0; m < MAXW; m++) acc[g][m] = fmaf(e, vv[m], acc[g][m]);
-                    }
+                for (int w = 0; w < MAXW; w++) o[g][w] = o[g][w] * corr + e * v[w];
+                m[g] = mn;
             }
-#pragma unroll
-            for (int g = 0; g < 8; g++)
-                if (g0b + g < G)
-#pragma unroll
-                    for (int m = 0; m < MAXW; m++)
-                        if (m < nw && lane + 32 * m < hd) red[(warp * G + g0b + g) * hd + lane + 32 * m] = acc[g][m];
         }
-        (void)GG;
+    }
+#pragma unroll
+    for (int g = 0; g < GMAX; g++) {
+        if (g < G) {
+            float *dst = wpart + (warp * GMAX + g) * stride;
+            if (lane == 0) dst[0] = m[g], dst[1] = l[g];
+#pragma unroll
+            for (int w = 0; w < MAXW; w++)
+                if (lane + 32 * w < hd) dst[2 + lane + 32 * w] = o[g][w];
+        }
     }
     __syncthreads();
-    for (int i = t; i < G * hd; i += AT) {
-        const float o = red[i] + red[G * hd + i] + red[2 * G * hd + i] + red[3 * G * hd + i];
+    for (int i = t; i < G * hd; i += AT) {  // merge the 4 warps
         const int g = i / hd, d = i % hd;
-        float *dst = p.part + ((int64_t)(g0 * G + g) * p.nsplit + split) * (hd + 2);
-        dst[2 + d] = o;
-        if (d == 0) dst[0] = ml[2 * g], dst[1] = ml[2 * g + 1];
-    }
-    // last CTA of this KV head merges the splits
-    __shared__ int is_last;
-    __threadfence();
-    __syncthreads();
-    if (t == 0) {
-        const int ticket = atomicAdd(&p.cnt[g0], 1);
-        is_last = ticket == p.nsplit - 1;
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    for (int i = t; i < G * hd; i += AT) {
-        const int g = i / hd, d = i % hd;
-        const float *base = p.part + (int64_t)(g0 * G + g) * p.nsplit * (hd + 2);
         float M = -INFINITY;
-        for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, base[s * (hd + 2)]);
-        float num = 0.0f, den = 0.0f;
-        for (int s = 0; s < p.nsplit; s++) {
-            const float *ps = base + s * (hd + 2);
-            const float w = ps[1] > 0.0f ? expf(ps[0] - M) : 0.0f;
-            num = fmaf(w, ps[2 + d], num);
-            den = fmaf(w, ps[1], den);
+        for (int w = 0; w < 4; w++) M = fmaxf(M, wpart[(w * GMAX + g) * stride]);
+        float lo = 0.0f, oo = 0.0f;
+        for (int w = 0; w < 4; w++) {
+            const float *src = wpart + (w * GMAX + g) * stride;
+            const float c = src[1] > 0.0f ? expf(src[0] - M) : 0.0f;
+            lo = fmaf(c, src[1], lo);
+            oo = fmaf(c, src[2 + d], oo);
         }
-        p.out[(int64_t)(g0 * G + g) * hd + d] = num / den;
+        float *dst = cpart + g * stride;
+        if (d == 0) dst[0] = M, dst[1] = lo;
+        dst[2 + d] = oo;
     }
-    if (t == 0) p.cnt[g0] = 0;
+    cluster.sync();  // every split's merged partial is visible cluster-wide
+    if (split == 0) {
+        for (int i = t; i < G * hd; i += AT) {
+            const int g = i / hd, d = i % hd;
+            float M = -INFINITY;
+            for (int r = 0; r < p.nsplit; r++) M = fmaxf(M, cluster.map_shared_rank(cpart, r)[g * stride]);
+            float num = 0.0f, den = 0.0f;
+            for (int r = 0; r < p.nsplit; r++) {
+                const float *src = cluster.map_shared_rank(cpart, r) + g * stride;
+                const float c = src[1] > 0.0f ? expf(src[0] - M) : 0.0f;
+                den = fmaf(c, src[1], den);
+                num = fmaf(c, src[2 + d], num);
+            }
+            p.out[(hq + g) * hd + d] = num / den;
+        }
+    }
     pdl_launch_dependents();
+    cluster.sync();  // rank 0 has finished reading the other CTAs' shared memory
+}
+
+template <int MAXW>
+int launch_t(const AttnPlan &a, const AParams &p, int n_kv_local, cudaStream_t s, bool pdl) {
+    auto fn = attn_decode_kernel<MAXW>;
+    QMC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    cudaLaunchConfig_t c = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = a.nsplit;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    c.gridDim = dim3(n_kv_local * p.gsplit, a.nsplit);
+    c.blockDim = dim3(AT);
+    c.dynamicSmemBytes = a.smem;
+    c.stream = s;
+    c.attrs = attr;
+    c.numAttrs = pdl ? 2 : 1;
+    QMC_CUDA(cudaLaunchKernelEx(&c, fn, p));
+    return QMC_OK;
 }
 
 }  // namespace
 
 AttnPlan plan_attention(int n_kv_local, int group, int hd, int max_seq, int num_sms) {
     AttnPlan a;
-    int ns = (2 * num_sms + n_kv_local - 1) / n_kv_local;
-    const int min_for_smem = (max_seq + 511) / 512;  // chunk <= 512 positions
-    if (ns < min_for_smem) ns = min_for_smem;
+    const int gsplit = (group + GMAX - 1) / GMAX;
+    int ns = (2 * num_sms + n_kv_local * gsplit - 1) / (n_kv_local * gsplit);
+    if (ns > 16) ns = 16;
     if (ns > max_seq) ns = max_seq;
     if (ns < 1) ns = 1;
     a.nsplit = ns;
     a.chunk_max = (max_seq + ns - 1) / ns;
-    a.smem = (size_t)(group * hd + group * a.chunk_max + 4 * group * hd + 2 * group) * 4;
-    a.part_floats = (size_t)n_kv_local * group * ns * (hd + 2);
-    (void)hd;
+    a.smem = (size_t)(5 * GMAX * (hd + 2)) * 4;
+    a.part_floats = 0;
     return a;
 }
 
 int launch_attention(const AttnPlan &a, const float *q, const float *kc, const float *vc, float *out, float *part,
                      int *cnt, const int *pos, int n_kv_local, int group, int hd, int kvl, cudaStream_t s, bool pdl) {
-    if (hd > 32 * MAXW || (hd & 1)) return set_error(QMC_EINVAL, "attention: head_dim %d unsupported", hd);
-    AParams p{q, kc, vc, out, part, cnt, pos, hd, group, kvl, a.nsplit, a.chunk_max, 1.0f / sqrtf((float)hd)};
-    if (a.smem > 48 * 1024)
-        QMC_CUDA(cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)a.smem));
-    cudaLaunchConfig_t c = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    c.gridDim = dim3(n_kv_local, a.nsplit);
-    c.blockDim = dim3(AT);
-    c.dynamicSmemBytes = a.smem;
-    c.stream = s;
-    c.attrs = pdl ? attr : nullptr;
-    c.numAttrs = pdl ? 1 : 0;
-    QMC_CUDA(cudaLaunchKernelEx(&c, attn_decode_kernel, p));
-    return QMC_OK;
+    (void)part;
+    (void)cnt;
+    if (hd > 256 || (hd & 1)) return set_error(QMC_EINVAL, "attention: head_dim %d unsupported", hd);
+    AParams p{q, kc, vc, out, pos, hd, group, (group + GMAX - 1) / GMAX, kvl, a.nsplit, 1.0f / sqrtf((float)hd)};
+    if (hd <= 32) return launch_t<1>(a, p, n_kv_local, s, pdl);
+    if (hd <= 64) return launch_t<2>(a, p, n_kv_local, s, pdl);
+    if (hd <= 128) return launch_t<4>(a, p, n_kv_local, s, pdl);
+    return launch_t<8>(a, p, n_kv_local, s, pdl);
 }
 
 }  // namespace qmc

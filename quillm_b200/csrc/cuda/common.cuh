@@ -110,6 +110,28 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
+// ---------------------------------------------------------------- greedy token selection
+// Order-preserving 64-bit key of (value, index): a larger value wins, equal values keep the lower
+// index -- the reference's first-maximum rule (src/sampler.c:27-32).  -0.0 counts as +0.0; NaN never wins.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = v == 0.0f ? 0u : __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (uint32_t)(0xffffffffu - (uint32_t)idx);
+}
+__device__ __forceinline__ int argmax_index(unsigned long long key) {
+    return key ? (int)(0xffffffffu - (uint32_t)(key & 0xffffffffu)) : 0;
+}
+// Device-resident generation state [token, pos, step, prompt length]: record the greedy token of step
+// s (from the last prompt token on), feed the next prompt token while the prompt lasts, advance pos.
+__device__ __forceinline__ void advance_state(int best, int *state, const int *forced, int *gen, int gen_cap) {
+    const int s = state[2], forced_n = state[3];
+    const int slot = s + 1 - forced_n;
+    if (gen && slot >= 0 && slot < gen_cap) gen[slot] = best;
+    state[0] = (s + 1 < forced_n) ? forced[s + 1] : best;
+    state[1] += 1;
+    state[2] = s + 1;
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }

@@ -103,18 +103,12 @@ __global__ void argmax_kernel(const float *__restrict__ x, int n, int *__restric
             int best = bi == 0x7fffffff ? 0 : bi;
             if (x[0] != x[0]) best = 0;  // a NaN in slot 0 is never replaced by the reference
             if (step_ctr) {
-                // device-resident generation: record the greedy token, then feed the next input token
-                // (the next prompt token while the prompt lasts) and advance the position
-                const int s = *step_ctr, forced_n = forced_n_ptr ? *forced_n_ptr : 0;
-                const int next_in = (s + 1 < forced_n) ? forced[s + 1] : best;
-                const int slot = s + 1 - forced_n;
-                if (tokens_out && slot >= 0 && slot < tokens_cap) tokens_out[slot] = best;
-                *out = next_in;
-                *step_ctr = s + 1;
+                // device-resident generation: state = {token, pos, step, prompt length}
+                advance_state(best, out, forced, tokens_out, tokens_cap);
             } else {
                 *out = best;
             }
-            if (advance_pos) *advance_pos += 1;
+            if (advance_pos && !step_ctr) *advance_pos += 1;
         }
     }
 }

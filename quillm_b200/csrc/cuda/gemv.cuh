@@ -9,6 +9,7 @@ enum GemvEpi : int {
     EPI_ADD = 1,     // y[r] += v            (residual add, src/model.c:179,186)
     EPI_QKV = 2,     // rows [0,Dq) -> q, [Dq,Dq+KVl) -> K-cache slot, rest -> V-cache slot; RoPE on q and k
     EPI_SWIGLU = 3,  // virtual row 2h = w1[h], 2h+1 = w3[h]; y[h] = silu(g) * u (src/ops.c:128-133)
+    EPI_LOGITS = 4,  // y[r] = v, plus the greedy argmax: the last CTA advances the generation state
 };
 
 struct GemvArgs {
@@ -27,6 +28,11 @@ struct GemvArgs {
     int Dq = 0, KVl = 0, hd = 0;
     const float2 *rope = nullptr;  // [max_seq][hd/2] (cos, sin) rounded to float exactly as src/ops.c:116-118
     const int *pos = nullptr;      // device position
+    // EPI_LOGITS: argmax key/ticket (zero between launches) and the generation state
+    unsigned long long *amax_key = nullptr;
+    int *amax_ctr = nullptr, *state = nullptr, *gen = nullptr;
+    const int *forced = nullptr;
+    int gen_cap = 0;
     // optional: also write the Q8_0 activation blocks (the qm_matvec xq scratch)
     void *xq_out = nullptr;
     int *err = nullptr;

@@ -50,6 +50,7 @@ struct qmc_model {
     float2 *rope = nullptr;
     int *state = nullptr;  // [0] token  [1] pos  [2] step  [3] prompt length
     int *forced = nullptr, *gen = nullptr, *attn_cnt = nullptr;
+    unsigned long long *amax = nullptr;  // [0] argmax key, [1] low 32 bits: CTA ticket (fused output argmax)
     int *h_state = nullptr;
     float *h_logits = nullptr;
     AttnPlan ap;
@@ -264,14 +265,24 @@ int enqueue_step(qmc_model *m) {
     g.x = m->x;
     g.norm_w = m->norm;
     g.eps = m->cfg.norm_eps;
-    g.epi = EPI_STORE;
     g.y = m->logits_l;
     g.err = c->err;
+    const bool fused = m->tp == 1 && m->dt_out != QMC_F32;
+    g.epi = fused ? EPI_LOGITS : EPI_STORE;
+    if (fused) {  // greedy argmax + state advance in the output GEMV's last CTA
+        g.amax_key = m->amax;
+        g.amax_ctr = (int *)(m->amax + 1);
+        g.state = m->state;
+        g.forced = m->forced;
+        g.gen = m->gen;
+        g.gen_cap = m->S;
+    }
     RC(launch_gemv(g, s, true));
     if (m->tp > 1)
         RC(nccl_check(ncclAllGather(m->logits_l, m->logits, m->Vl, ncclFloat, m->comm, s), "all-gather(logits)"));
-    RC(launch_argmax(m->logits, m->V, m->state, s, true, m->state + 1, m->forced, m->state + 3, m->state + 2, m->gen,
-                     m->S));
+    if (!fused)
+        RC(launch_argmax(m->logits, m->V, m->state, s, true, m->state + 1, m->forced, m->state + 3, m->state + 2,
+                         m->gen, m->S));
     return QMC_OK;
 }
 
@@ -358,7 +369,8 @@ int qmc_model_create(const qmc_config *cfg, int tp_rank, int tp_size, const void
         (rc = dalloc(m, (void **)&m->vc, kvbytes)) || (rc = dalloc(m, (void **)&m->attn_part, m->ap.part_floats * 4)) ||
         (rc = dalloc(m, (void **)&m->attn_cnt, (size_t)m->NKVl * 4)) ||
         (rc = dalloc(m, (void **)&m->rope, (size_t)m->S * (hd / 2) * 8)) || (rc = dalloc(m, (void **)&m->state, 16)) ||
-        (rc = dalloc(m, (void **)&m->forced, (size_t)m->S * 4)) || (rc = dalloc(m, (void **)&m->gen, (size_t)m->S * 4)))
+        (rc = dalloc(m, (void **)&m->forced, (size_t)m->S * 4)) || (rc = dalloc(m, (void **)&m->gen, (size_t)m->S * 4)) ||
+        (rc = dalloc(m, (void **)&m->amax, 16)))
         return fail(rc);
     m->logits_l = tp_size > 1 ? nullptr : m->logits;
     if (tp_size > 1 && (rc = dalloc(m, (void **)&m->logits_l, (size_t)m->Vl * 4))) return fail(rc);
@@ -366,7 +378,8 @@ int qmc_model_create(const qmc_config *cfg, int tp_rank, int tp_size, const void
         return fail(set_error(QMC_ENOMEM, "pinned host buffers"));
     // zeroed caches/counters, RoPE table from the reference's double expressions
     if (cudaMemsetAsync(m->kc, 0, kvbytes, m->stream) || cudaMemsetAsync(m->vc, 0, kvbytes, m->stream) ||
-        cudaMemsetAsync(m->attn_cnt, 0, (size_t)m->NKVl * 4, m->stream) || cudaMemsetAsync(m->state, 0, 16, m->stream))
+        cudaMemsetAsync(m->attn_cnt, 0, (size_t)m->NKVl * 4, m->stream) || cudaMemsetAsync(m->state, 0, 16, m->stream) ||
+        cudaMemsetAsync(m->amax, 0, 16, m->stream))
         return fail(set_error(QMC_ECUDA, "memset"));
     std::vector<float> tab((size_t)m->S * hd);
     for (int p = 0; p < m->S; p++) rope_row_host(p, hd, k.rope_theta, tab.data() + (size_t)p * hd);
