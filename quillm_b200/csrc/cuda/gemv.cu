@@ -8,14 +8,19 @@
 // release them through per-stage "empty" mbarriers.  No CTA-wide barrier runs inside the stream loop.
 //
 // Work split: a CTA owns a contiguous range of units (a unit is one row, or the row pair of the RoPE /
-// SwiGLU epilogues) and one consumer warp owns each unit of a 16-unit row group.  Rows are streamed in
-// K-chunks of C blocks (one bulk copy per row chunk), so a stage stays near 18 KB whatever the row
-// length; a warp accumulates its row across the chunk stages and reduces once, at the row's end.
-// Activations are quantized once per CTA into shared memory (int8, fp32 scale, block sum).  Per block:
-// aligned 32-bit shared loads + funnel shifts realign the 2-byte-aligned block, dp4a forms the integer
-// block dot, s += (float)acc * (dW * dX) as in the reference (src/kernels_scalar.c:12-34).  Q4_0 uses
-// sum (n_i - 8) x_i = sum n_i x_i - 8 sum x_i with nibbles fed to dp4a against even/odd-permuted
-// activations.
+// SwiGLU epilogues).  A stage is R whole units copied by ONE bulk copy of ~16-20 KB (many small copies
+// per stage cost ~50 TMA cycles each and halve the stream rate).  The 16 consumer warps form 4 groups
+// of 4 and group j owns stages j, j+4, j+8, ...: each stage's processing is a chain of dependent
+// steps (~0.3-0.5 us even for trivial work), and with all warps on every stage that chain gated every
+// refill (measured 2.4-2.8 TB/s); four stages in flight through four groups hide it.  Inside a group a
+// warp owns whole units when a stage has >= 4 of them, otherwise g = 4/R warps share a unit's blocks and
+// meet in shared memory behind a group-local named barrier.  Activations are quantized once per CTA into
+// shared memory (int8 in a bank-swizzled layout, fp32 scale, block sum).  Per block: aligned 32-bit
+// shared loads + funnel shifts realign the 2-byte-aligned block, dp4a forms the integer block dot and
+// s += (float)acc * (dW * dX) as in the reference (src/kernels_scalar.c:12-34).  Q4_0 feeds the low
+// nibbles (x 1) and the masked high nibbles (x 16, unsigned) to dp4a against even/odd-permuted
+// activations and removes the offset with sum (n_i - 8) x_i = sum n_i x_i - 8 sum x_i.  The footprint
+// stays under ~112 KB of shared memory and 60 registers so the next kernel's CTA can co-reside.
 #include <stdio.h>
 
 #include "gemv.cuh"
@@ -24,9 +29,10 @@ namespace qmc {
 namespace {
 
 constexpr int NCW = 16;              // consumer warps
+constexpr int NG = 4, GW = 4;        // consumer groups x warps per group (NG * GW == NCW)
 constexpr int NT = (NCW + 1) * 32;   // + one producer warp
 constexpr int CH = 4096;             // activation staging chunk (floats)
-constexpr int kStageBudget = 24 * 1024;
+constexpr int kStageTarget = 16 * 1024;
 constexpr int kCoResidentSmem = 112 * 1024;  // two CTAs (this kernel and the next) per SM
 
 struct KParams {
@@ -34,10 +40,9 @@ struct KParams {
     int64_t w_bytes;  // readable bytes of W0 (and of W1)
     int64_t units;    // rows, or row pairs for the paired epilogues
     int K, nb, rb;
-    int urows;        // rows per unit in shared memory (2 for QKV pairs and for SwiGLU's w1/w3 rows)
-    int chunked;      // 1: per-row chunk copies (row bytes % 16 == 0); 0: whole rows, one copy per stage
-    int C, nchunks, slot_bytes;  // blocks per chunk, chunks per row, bytes per row slot (chunked mode)
-    int stage_bytes, nstages;
+    int urows;        // rows per unit (2 for QKV pairs and for SwiGLU's w1/w3 rows)
+    int R, g;         // units per stage; warps per unit (g = 4 / R when R < 4, else 1)
+    int stage_bytes, part_bytes, nstages;  // part_bytes: offset of the w3 copy inside a SwiGLU stage
     int off_bars, off_xq, off_xds, off_xs, off_red;  // shared-memory offsets
     const float *x, *norm_w;
     float eps;
@@ -71,28 +76,11 @@ __device__ __forceinline__ CopyPlan plan_copy(int64_t start, int64_t len, int64_
     return c;
 }
 
-// source row `i` (0..urows-1) of unit u
-__device__ __forceinline__ const uint8_t *unit_row(const KParams &p, int64_t u, int i) {
-    if (p.W1) return (i ? p.W1 : p.W0) + u * p.rb;
-    return p.W0 + (u * p.urows + i) * p.rb;
-}
-
-// stage k of a CTA whose units start at u0: row group k / nchunks, chunk k % nchunks
+// stage k of a CTA whose units start at u0: units [u0 + kR, u0 + kR + R) as one contiguous copy (two for
+// SwiGLU's separate w1/w3 matrices), 16-byte lines by bulk copy plus tail bytes by plain stores
 __device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int64_t u0, int64_t u1, int k) {
-    const int64_t ua = u0 + (int64_t)(k / p.nchunks) * NCW;
-    const int64_t n = min((int64_t)NCW, u1 - ua);
-    constexpr int BS_Q8 = kQ8Bytes;
-    const int BS = p.rb / p.nb == BS_Q8 ? kQ8Bytes : kQ4Bytes;
-    if (p.chunked) {
-        const int c = k % p.nchunks, cb0 = c * p.C, cb1 = min(p.nb, cb0 + p.C);
-        const uint32_t bytes = (uint32_t)((cb1 - cb0) * BS);
-        mbar_arrive_tx(bar, bytes * (uint32_t)(n * p.urows));
-        for (int64_t j = 0; j < n; j++)
-            for (int i = 0; i < p.urows; i++)
-                bulk_g2s(stage + (j * p.urows + i) * p.slot_bytes, unit_row(p, ua + j, i) + (int64_t)cb0 * BS, bytes, bar);
-        return;
-    }
-    // whole rows: contiguous units (two runs for SwiGLU's separate matrices), 16-byte lines + tail bytes
+    const int64_t ua = u0 + (int64_t)k * p.R;
+    const int64_t n = min((int64_t)p.R, u1 - ua);
     const uint8_t *src[2];
     uint8_t *dst[2];
     CopyPlan cp[2];
@@ -100,18 +88,22 @@ __device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int
     if (p.W1) {
         parts = 2;
         src[0] = p.W0, src[1] = p.W1;
-        dst[0] = stage, dst[1] = stage + p.stage_bytes / 2;
+        dst[0] = stage, dst[1] = stage + p.part_bytes;
         cp[0] = cp[1] = plan_copy(ua * p.rb, n * p.rb, p.w_bytes);
     } else {
         src[0] = p.W0, dst[0] = stage;
         cp[0] = plan_copy(ua * p.urows * p.rb, n * p.urows * p.rb, p.w_bytes);
     }
     uint32_t tx = 0;
+    bool plain = false;
     for (int i = 0; i < parts; i++) {
         for (int64_t b = cp[i].tail0; b < cp[i].end; b++) dst[i][b - cp[i].a0] = src[i][b];
+        plain |= cp[i].tail0 < cp[i].end;
         tx += cp[i].tma;
     }
-    fence_proxy_async();
+    // only bytes stored by this thread need ordering against the async copies into the same stage; an
+    // unconditional proxy fence here serialises the ring (measured: ~2 TB/s instead of ~7 TB/s)
+    if (plain) fence_proxy_async();
     mbar_arrive_tx(bar, tx);
     for (int i = 0; i < parts; i++)
         if (cp[i].tma) bulk_g2s(dst[i], src[i] + cp[i].a0, cp[i].tma, bar);
@@ -119,6 +111,9 @@ __device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ---------------------------------------------------------------- per-block dots from shared memory
@@ -131,13 +126,20 @@ __device__ __forceinline__ void load_words(const uint8_t *bp, uint32_t (&w)[NW],
     for (int i = 0; i < NW; i++) w[i] = wp[i];
 }
 
-// 32 activation bytes of block b as 8 words; quarter-warps alternate halves to stay conflict-free
-__device__ __forceinline__ void load_x(const uint8_t *xq, int b, int lane, uint32_t (&xw)[8]) {
-    const uint4 *p = (const uint4 *)(xq + (int64_t)b * 32);
-    const int h = (lane >> 2) & 1;
-    const uint4 a = p[h], c = p[h ^ 1];
-    const uint4 lo = h ? c : a, hi = h ? a : c;
+// 32 activation bytes of block b as 8 words.  The prologue stores the two 16-byte halves of block b
+// swapped when bit 2 of b is set, so the 8 lanes of a quarter-warp (consecutive b) hit all 32 banks.
+__device__ __forceinline__ int xswz(int b) { return ((b >> 2) & 1) << 4; }
+__device__ __forceinline__ void load_x(const uint8_t *xq, int b, uint32_t (&xw)[8]) {
+    const uint8_t *p = xq + (int64_t)b * 32;
+    const int sw = xswz(b);
+    const uint4 lo = *(const uint4 *)(p + sw), hi = *(const uint4 *)(p + (sw ^ 16));
     xw[0] = lo.x, xw[1] = lo.y, xw[2] = lo.z, xw[3] = lo.w, xw[4] = hi.x, xw[5] = hi.y, xw[6] = hi.z, xw[7] = hi.w;
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsigned a bytes x signed b bytes
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
 template <int DT>
@@ -154,14 +156,14 @@ __device__ __forceinline__ float block_dot(const uint8_t *bp, const uint32_t (&x
         uint32_t w[5], sh;
         load_words<5>(bp, w, sh);
         const uint32_t dbits = __funnelshift_r(w[0], w[1], sh) & 0xffffu;
-        int acc = 0;
+        int lo = 0, hi16 = 0;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const uint32_t qw = __funnelshift_rc(w[i], w[i + 1], 16u + sh);
-            acc = __dp4a((int)(qw & 0x0f0f0f0fu), (int)xw[i], acc);          // even elements
-            acc = __dp4a((int)((qw >> 4) & 0x0f0f0f0fu), (int)xw[4 + i], acc);  // odd elements
+            lo = __dp4a((int)(qw & 0x0f0f0f0fu), (int)xw[i], lo);      // even elements
+            hi16 = dp4a_us(qw & 0xf0f0f0f0u, xw[4 + i], hi16);         // odd elements, x16
         }
-        acc -= 8 * xs;
+        const int acc = lo + (hi16 >> 4) - 8 * xs;
         return (float)acc * (h2f(dbits) * xd);
     }
 }
@@ -262,7 +264,7 @@ __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
             uint32_t dh;
             const int qv = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
             const int pos_in_block = DT == QMC_Q4_0 ? ((lane & 1) ? 16 : 0) + (lane >> 3) * 4 + ((lane & 7) >> 1) : lane;
-            xq[b * 32 + pos_in_block] = (uint8_t)(int8_t)qv;
+            xq[b * 32 + (pos_in_block ^ xswz(b))] = (uint8_t)(int8_t)qv;
             const int bs = __reduce_add_sync(0xffffffffu, qv);
             if (lane == 0) xds[b] = make_int2(__float_as_int(dd), bs);
             if (p.xq_out) {
@@ -278,9 +280,9 @@ __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
 // EPI_LOGITS tail (consumer warps only): CTA max of the warps' keys, one atomicMax per CTA, and the
 // last CTA to finish (ticket) turns the global maximum into the next token and resets key and ticket.
 __device__ void logits_argmax(const KParams &p, uint8_t *sm, unsigned long long best, int warp, int lane) {
-    unsigned long long *keys = (unsigned long long *)(sm + p.off_red);
+    unsigned long long *keys = (unsigned long long *)(sm + p.off_red + 4 * NCW * 4);
     if (lane == 0) keys[warp] = best;
-    asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+    named_sync(15, NCW * 32);  // ids 1..8 belong to the unit groups
     if (warp == 0 && lane == 0) {
         unsigned long long k = 0;
         for (int w = 0; w < NCW; w++) k = max(k, keys[w]);
@@ -305,12 +307,12 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t u0 = (int64_t)blockIdx.x * p.units / gridDim.x;
     const int64_t u1 = (int64_t)(blockIdx.x + 1) * p.units / gridDim.x;
-    const int nst = (int)((u1 - u0 + NCW - 1) / NCW) * p.nchunks;  // stages this CTA streams
+    const int nst = (int)((u1 - u0 + p.R - 1) / p.R);  // stages this CTA streams
 
     if (t == 0) {
         for (int s = 0; s < p.nstages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
+            mbar_init(&empty[s], GW);
         }
         fence_mbar_init();
     }
@@ -338,54 +340,56 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
     constexpr int BS = DT == QMC_Q8_0 ? kQ8Bytes : kQ4Bytes;
     const uint8_t *xq = sm + p.off_xq;
     const int2 *xds = (const int2 *)(sm + p.off_xds);
+    float2 *red = (float2 *)(sm + p.off_red);  // [2][NCW] partial sums of shared units, double-buffered
     const int pos = p.epi == EPI_QKV ? *p.pos : 0;
     const bool two = p.urows == 2;
-    float a0 = 0.0f, a1 = 0.0f;
+    const int grp = warp / GW, wig = warp % GW;
+    const int g = p.g, sub = wig % g, bstep = 32 * g;
     unsigned long long best = 0;
-    for (int k = 0; k < nst; k++) {
-        const int s = k % p.nstages, c = k % p.nchunks;
+    for (int k = grp; k < nst; k += NG) {  // this group's stages
+        const int s = k % p.nstages;
         if (!mbar_wait(&full[s], (uint32_t)(k / p.nstages) & 1u)) {
             if (lane == 0) raise_error(p.err, kErrMbarTimeout);
             return;
         }
-        const int64_t ua = u0 + (int64_t)(k / p.nchunks) * NCW, unit = ua + warp;
-        if (unit < u1) {
-            const uint8_t *stage = sm + (int64_t)s * p.stage_bytes;
+        const int64_t ua = u0 + (int64_t)k * p.R;
+        const int n = (int)min((int64_t)p.R, u1 - ua);
+        const uint8_t *stage = sm + (int64_t)s * p.stage_bytes;
+        // g == 1: warp wig takes units wig, wig+4, ...; g > 1: the g warps of unit wig / g share it
+        for (int i = g == 1 ? wig : wig / g; i < n; i += g == 1 ? GW : n) {
+            const int64_t unit = ua + i;
             const uint8_t *r0, *r1;
-            int cb0, cb1;
-            if (p.chunked) {
-                r0 = stage + (int64_t)warp * p.urows * p.slot_bytes;
-                r1 = r0 + p.slot_bytes;
-                cb0 = c * p.C;
-                cb1 = min(p.nb, cb0 + p.C);
-                r0 -= (int64_t)cb0 * BS;  // index blocks by their row position
-                r1 -= (int64_t)cb0 * BS;
-            } else if (p.W1) {
+            if (p.W1) {
                 const int64_t off = (ua * p.rb) & 15;
-                r0 = stage + off + (int64_t)warp * p.rb;
-                r1 = stage + p.stage_bytes / 2 + off + (int64_t)warp * p.rb;
-                cb0 = 0, cb1 = p.nb;
+                r0 = stage + off + (int64_t)i * p.rb;
+                r1 = stage + p.part_bytes + off + (int64_t)i * p.rb;
             } else {
-                r0 = stage + ((ua * p.urows * p.rb) & 15) + (int64_t)warp * p.urows * p.rb;
+                r0 = stage + ((ua * p.urows * p.rb) & 15) + (int64_t)i * p.urows * p.rb;
                 r1 = r0 + p.rb;
-                cb0 = 0, cb1 = p.nb;
             }
-            for (int b = cb0 + lane; b < cb1; b += 32) {
+            float a0 = 0.0f, a1 = 0.0f;
+            for (int b = sub * 32 + lane; b < p.nb; b += bstep) {
                 uint32_t xw[8];
-                load_x(xq, b, lane, xw);
+                load_x(xq, b, xw);
                 const int2 ds = xds[b];
                 const float xd = __int_as_float(ds.x);
                 a0 += block_dot<DT>(r0 + b * BS, xw, xd, ds.y);
                 if (two) a1 += block_dot<DT>(r1 + b * BS, xw, xd, ds.y);
             }
-            if (c == p.nchunks - 1) {  // row complete
-                a0 = warp_sum(a0);
-                if (two) a1 = warp_sum(a1);
-                if (lane == 0) {
-                    epilogue(p, unit, a0, a1, pos);
-                    if (p.epi == EPI_LOGITS && a0 == a0) best = max(best, argmax_key(a0, (int)unit));
+            a0 = warp_sum(a0);
+            if (two) a1 = warp_sum(a1);
+            if (g > 1) {
+                float2 *rb = red + ((k / NG) & 1) * NCW;
+                if (lane == 0) rb[warp] = make_float2(a0, a1);
+                named_sync(1 + grp * (GW / g) + i, 32 * g);  // ids 1..8: per (group, shared unit)
+                if (sub == 0 && lane == 0) {
+                    a0 = a1 = 0.0f;
+                    for (int w = 0; w < g; w++) a0 += rb[warp + w].x, a1 += rb[warp + w].y;
                 }
-                a0 = a1 = 0.0f;
+            }
+            if (sub == 0 && lane == 0) {
+                epilogue(p, unit, a0, a1, pos);
+                if (p.epi == EPI_LOGITS && a0 == a0) best = max(best, argmax_key(a0, (int)unit));
             }
         }
         __syncwarp();
@@ -507,33 +511,32 @@ int launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl, int grid_limit
         return QMC_OK;
     }
 
-    // stage = 16 units x (urows rows) x (C blocks); rows whose byte length is a multiple of 16 stream as
-    // per-row chunk copies, others as whole contiguous rows
+    // stage = R whole units in one copy: the smallest power-of-two R (R * g = 16) whose stage reaches
+    // kStageTarget bytes; very long units stream one per stage with all 16 warps on it
     p.urows = (a.epi == EPI_QKV || a.epi == EPI_SWIGLU) ? 2 : 1;
-    const int BS = a.dtype == QMC_Q8_0 ? kQ8Bytes : kQ4Bytes;
-    p.chunked = (p.nb % 8) == 0;
-    if (p.chunked) {
-        p.C = 256;
-        while (p.C > 32 && (int64_t)NCW * p.urows * p.C * BS > kStageBudget) p.C /= 2;
-        if (p.C > p.nb) p.C = (p.nb + 31) / 32 * 32;
-        p.nchunks = (p.nb + p.C - 1) / p.C;
-        p.slot_bytes = p.C * BS;  // multiple of 16 (C is a multiple of 8 blocks)
-        p.stage_bytes = (int)(((int64_t)NCW * p.urows * p.slot_bytes + 127) & ~(int64_t)127);
+    const int64_t unit_bytes = (int64_t)p.urows * p.rb;
+    p.R = 1;
+    while (p.R < 64 && (int64_t)p.R * unit_bytes < kStageTarget) p.R *= 2;
+    p.g = p.R >= GW ? 1 : GW / p.R;
+    if (p.W1) {
+        p.part_bytes = (int)(((int64_t)p.R * p.rb + 48 + 127) & ~(int64_t)127);
+        p.stage_bytes = 2 * p.part_bytes;
     } else {
-        p.C = p.nb;
-        p.nchunks = 1;
-        p.slot_bytes = 0;
-        const int64_t part = ((int64_t)NCW * (p.W1 ? 1 : p.urows) * p.rb + 48 + 127) & ~(int64_t)127;
-        p.stage_bytes = (int)(p.W1 ? 2 * part : part);
+        p.part_bytes = 0;
+        p.stage_bytes = (int)(((int64_t)p.R * unit_bytes + 48 + 127) & ~(int64_t)127);
     }
     const int xq_bytes = ((p.nb * 32 + 127) / 128) * 128, xds_bytes = ((p.nb * 8 + 127) / 128) * 128;
-    const int fixed = xq_bytes + xds_bytes + CH * 4 + 2 * NT * 4 + 256;
+    const int fixed = xq_bytes + xds_bytes + CH * 4 + 2 * NT * 4 + 256;  // red: 2 x 16 float2 + 16 keys
     // prefer a footprint that lets the next kernel's CTA co-reside (its weight prefetch then overlaps this
     // kernel's tail); very long rows fall back to the whole shared memory of the SM
+    // nstages is a multiple of NG so every slot belongs to one group (slot s serves stages s, s + ns, ...,
+    // all of group s % NG).  A slot shared by two groups breaks the parity waits: a group that runs one
+    // ring lap ahead of the group before it sees the previous phase's parity as complete and reads a
+    // slot whose copy has not landed.
     int ns = (kCoResidentSmem - fixed - 256) / p.stage_bytes;
-    if (ns < 3) ns = ((int)c->max_smem_optin - fixed - 256) / p.stage_bytes;
-    if (ns > 6) ns = 6;
-    if (ns < 2) return set_error(QMC_EINVAL, "gemv: K=%lld needs more shared memory than a CTA has", (long long)a.K);
+    if (ns < NG) ns = ((int)c->max_smem_optin - fixed - 256) / p.stage_bytes;
+    ns = ns >= 2 * NG ? 2 * NG : ns >= NG ? NG : 0;
+    if (ns == 0) return set_error(QMC_EINVAL, "gemv: K=%lld needs more shared memory than a CTA has", (long long)a.K);
     p.nstages = ns;
     p.off_bars = ns * p.stage_bytes;
     p.off_xq = p.off_bars + ((2 * ns * 8 + 127) / 128) * 128;
