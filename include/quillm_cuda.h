@@ -77,6 +77,19 @@ int qmc_matmul_nt(const float *A, const float *B, float *C, int64_t M, int64_t N
 int qmc_matmul_nt_q(int dtype, const void *W, const float *A, float *C, int64_t T, int64_t N, int64_t K,
                     void *stream);
 
+/* Same result as qmc_matmul_nt_q, for callers that cannot call cudaMalloc -- code running while a CUDA
+ * graph is being captured, or a host application that owns all device memory through its own allocator
+ * and forbids a library from allocating.  No counterpart in the reference.  Allocates nothing: the
+ * Q8_0-quantized rows of A go to one fixed 8 MiB array in the library's static device memory (held by
+ * every GPU that loads the library until the process exits), so T * ceil(K/32) * 36 bytes must fit in
+ * 8 MiB (e.g. T = 512 at K = 11008); larger calls return QMC_EINVAL.  The first call on a device looks
+ * the array's address up (cudaGetSymbolAddress) and should come before any stream capture.  All calls
+ * on a device share the array and each call overwrites it before reading it: two calls whose executions
+ * overlap on the GPU (for example on two unsynchronised streams) race.  stream NULL means the CUDA
+ * default stream. */
+int qmc_matmul_nt_q_noalloc(int dtype, const void *W, const float *A, float *C, int64_t T, int64_t N, int64_t K,
+                            void *stream);
+
 /* ---- elementwise, in place on device buffers (src/ops.c:93-133) ---- */
 int qmc_rmsnorm(float *out, const float *x, const float *w, int64_t n, float eps, void *stream);
 int qmc_softmax(float *x, int64_t n, void *stream);

@@ -226,6 +226,60 @@ int qmc_matmul_nt_q(int dtype, const void *W, const float *A, float *C, int64_t 
     return launch_matmul_q(dtype, W, aq, ad, C, T, N, K, s);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free prefill
+// qmc_matmul_nt_q needs T * ceil(K/32) * 36 bytes of device scratch for the Q8_0-quantized rows of A
+// and grows a cudaMalloc'd buffer for them.  The variant below takes that scratch from one fixed array
+// in the library's static device memory instead, for callers that must not allocate (see the header).
+namespace {
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // 8 MiB on every GPU that loads the library
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+void *g_noalloc_addr[64];
+std::mutex g_noalloc_mu;
+
+// device address of g_noalloc_scratch on the current device, looked up once per device (the array's
+// host-side name is only a stand-in; a kernel must be given this address)
+int noalloc_scratch(void **out) {
+    int d = 0;
+    QMC_CUDA(cudaGetDevice(&d));
+    if (d < 0 || d >= 64) return set_error(QMC_EINVAL, "device %d out of range", d);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[d]) {
+        void *p = nullptr;
+        QMC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_addr[d] = p;
+    }
+    *out = g_noalloc_addr[d];
+    return QMC_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qmc_matmul_nt_q_noalloc(int dtype, const void *W, const float *A, float *C, int64_t T, int64_t N, int64_t K,
+                            void *stream) {
+    if (T <= 0 || N <= 0) return QMC_OK;
+    if (!W || !A || !C || K <= 0) return set_error(QMC_EINVAL, "matmul_nt_q_noalloc: bad arguments");
+    cudaStream_t s = (cudaStream_t)stream;  // NULL: the CUDA default stream (no library stream is created)
+    if (dtype == QMC_F32) return launch_gemm_f32(A, (const float *)W, C, T, N, K, s);
+    if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "matmul_nt_q_noalloc: bad dtype %d", dtype);
+    const int64_t nb = nblocks(K);
+    const size_t qbytes = (size_t)(T * nb * 32 + 255) / 256 * 256, need = qbytes + (size_t)T * nb * 4;
+    if (need > kNoAllocScratchBytes)
+        return set_error(QMC_EINVAL,
+                         "matmul_nt_q_noalloc: T=%lld x K=%lld needs %zu bytes of scratch, above the fixed %zu "
+                         "(T * ceil(K/32) * 36 must stay within it; split T or use qmc_matmul_nt_q)",
+                         (long long)T, (long long)K, need, kNoAllocScratchBytes);
+    void *scr = nullptr;
+    int rc = noalloc_scratch(&scr);
+    if (rc) return rc;
+    int8_t *aq = (int8_t *)scr;
+    float *ad = (float *)((uint8_t *)scr + qbytes);
+    if ((rc = launch_quantize_act(A, T, K, aq, ad, s))) return rc;  // overwrites every byte it reads later
+    return launch_matmul_q(dtype, W, aq, ad, C, T, N, K, s);
+}
+
 int qmc_rmsnorm(float *out, const float *x, const float *w, int64_t n, float eps, void *stream) {
     CTX_OR_FAIL();
     if (n <= 0) return QMC_OK;
