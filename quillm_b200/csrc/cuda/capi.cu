@@ -140,6 +140,8 @@ int qmc_check_device_error(void) {
     QMC_CUDA(cudaMemcpy(&v, c_->err, sizeof v, cudaMemcpyDeviceToHost));
     if (v) {
         QMC_CUDA(cudaMemset(c_->err, 0, sizeof(int)));
+        if (v & kErrBadState)
+            return set_error(QMC_EINVAL, "a decode step found its device position or token out of range (code %d)", v);
         return set_error(QMC_ETIMEOUT, "a device-side bounded wait expired (code %d)", v);
     }
     return QMC_OK;

@@ -68,7 +68,7 @@ __device__ __forceinline__ int quant_lane(float v, float qmax, int qmin, int qma
 // ---------------------------------------------------------------- error word
 // Kernels whose spin-waits expire OR a code into *err and return; the host reads it with
 // qmc_check_device_error().
-enum : int { kErrMbarTimeout = 1, kErrFlagTimeout = 2 };
+enum : int { kErrMbarTimeout = 1, kErrFlagTimeout = 2, kErrBadState = 4 };
 __device__ __forceinline__ void raise_error(int *err, int code) {
     if (err) atomicOr(err, code);
 }

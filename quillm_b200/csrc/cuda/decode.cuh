@@ -1,0 +1,74 @@
+// Persistent whole-step decode kernel: one launch runs every matvec, attention and the greedy argmax
+// of a decode step (tensor-parallel size 1, Q8_0 / Q4_0 weights in the split-row layout below).
+#pragma once
+#include "common.cuh"
+
+namespace qmc {
+
+// Split-row layout of a quantized matrix: each row is its ceil(K/32) fp16 block scales (padded to a
+// 16-byte multiple) followed by the blocks' quant bytes (16 per Q4_0 block, 32 per Q8_0 block), so every
+// row and every block payload is 16-byte aligned.  Same numbers as the file's AoS blocks, regrouped.
+__host__ __device__ inline int64_t split_scale_bytes(int64_t K) { return ((nblocks(K) * 2 + 15) / 16) * 16; }
+__host__ __device__ inline int64_t split_row_bytes(int dtype, int64_t K) {
+    return split_scale_bytes(K) + nblocks(K) * (dtype == QMC_Q8_0 ? 32 : 16);
+}
+// AoS rows (file layout) -> split rows; row r goes to dst + r * dst_stride
+int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, void *dst, int64_t dst_stride,
+                        cudaStream_t s);
+
+constexpr int kDecodeHeadsPerUnit = 4;  // query heads per attention work unit
+
+enum DecodePhaseKind : int { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_W2 = 4, PH_OUT = 5 };
+
+struct DecodePhase {
+    int kind;             // DecodePhaseKind
+    int dtype;            // weights: QMC_Q8_0 / QMC_Q4_0
+    const uint8_t *W;     // split-row matrix; QKV rows q|k|v, FFN rows w1[0], w3[0], w1[1], ...
+    int64_t units;        // units: rows (WO, W2, OUT) or row pairs (QKV RoPE pairs, FFN w1/w3 pairs)
+    int K, nb, urows;     // columns, blocks per row, rows per unit
+    int rbytes, sbytes;   // split-row bytes per row, scale bytes per row
+    int R;                // units per ring stage
+    int embed;            // input is the current token's embedding row (first phase)
+    const float *in;      // input vector (x, attention output, SwiGLU output)
+    const float *norm_w;  // fused rmsnorm weight or null
+    float *out;           // WO/W2: x (+=), FFN: h, OUT: logits
+    float *kc, *vc;       // QKV / ATTN: this layer's caches [max_seq][KVl]
+};
+
+struct DecodeParams {
+    const DecodePhase *ph;
+    int nph;
+    int D, Dq, KVl, hd, nkv, group, gsplit;  // attention geometry (gsplit: CTAs per KV head's query group)
+    float eps, scale;
+    const uint8_t *tok;  // embedding table (file layout)
+    int dt_tok;
+    float *x;  // residual stream
+    float *q, *xb;
+    const float2 *rope;
+    int *state;  // [token, pos, step, prompt length]
+    int vocab;   // valid tokens [0, vocab)
+    const int *forced;
+    int *gen;
+    int gen_cap;
+    unsigned long long *amax_key;
+    int *amax_ctr;
+    unsigned int *gbar;  // grid barrier: [0] arrivals, [1] generation
+    float *apart;        // attention partials [nkv * gsplit][maxseg][4][hd + 2]
+    int *acnt;           // attention merge tickets [nkv * gsplit]
+    int maxseg;
+    int *err;
+    int nslots, slot_bytes;
+    int off_bars, off_xq, off_xds, off_red;
+};
+
+struct DecodePlan {
+    int nslots = 0, slot_bytes = 0, off_bars = 0, off_xq = 0, off_xds = 0, off_red = 0;
+    size_t smem = 0;
+};
+// ring / shared-memory plan for the largest unit and activation length of the model; false if the
+// model does not fit (then the per-kernel path is used)
+bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out);
+// one CTA per SM, cooperative (all CTAs co-resident for the grid barriers)
+int launch_decode(const DecodeParams &p, const DecodePlan &plan, int grid, cudaStream_t s);
+
+}  // namespace qmc

@@ -267,7 +267,7 @@ __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
             xq[b * 32 + (pos_in_block ^ xswz(b))] = (uint8_t)(int8_t)qv;
             const int bs = __reduce_add_sync(0xffffffffu, qv);
             if (lane == 0) xds[b] = make_int2(__float_as_int(dd), bs);
-            if (p.xq_out) {
+            if (p.xq_out && blockIdx.x == 0) {  // every CTA holds the same blocks; one writes them
                 uint8_t *blk = p.xq_out + (int64_t)b * kQ8Bytes;
                 blk[2 + lane] = (uint8_t)(int8_t)qv;
                 if (lane == 0) blk[0] = (uint8_t)(dh & 0xff), blk[1] = (uint8_t)(dh >> 8);

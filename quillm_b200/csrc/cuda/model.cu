@@ -16,9 +16,11 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "attention.cuh"
+#include "decode.cuh"
 #include "elementwise.cuh"
 #include "gemv.cuh"
 #include "synth.cuh"
@@ -29,6 +31,7 @@ namespace {
 struct Layer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     uint8_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w3 = nullptr, *w2 = nullptr;
+    uint8_t *sqkv = nullptr, *swo = nullptr, *s13 = nullptr, *sw2 = nullptr;  // split-row copies (persistent path)
     int dt[12];  // dtype per uploaded kind (indices QMC_T_*), -1 = missing
 };
 }  // namespace
@@ -56,6 +59,16 @@ struct qmc_model {
     AttnPlan ap;
     cudaGraphExec_t graph = nullptr;
     bool have_tok = false, have_norm = false, have_out = false;
+    // persistent decode path (tp 1, quantized matrices): split-row weights, phase list, barrier state
+    bool mega = false, mega_checked = false, repacked = false;
+    DecodePlan plan;
+    std::vector<DecodePhase> phases;
+    DecodePhase *d_phases = nullptr;
+    uint8_t *sout = nullptr;
+    unsigned *gbar = nullptr;
+    float *apart = nullptr;
+    int *acnt = nullptr;
+    int maxseg = 1, gsplit = 1;
 };
 
 namespace {
@@ -190,10 +203,151 @@ int nccl_check(ncclResult_t r, const char *what) {
     return set_error(QMC_ENCCL, "%s: %s", what, ncclGetErrorString(r));
 }
 
+// ---------------------------------------------------------------- persistent decode path
+// Eligible when one GPU holds the model, every matrix is Q8_0/Q4_0 and the ring plan fits shared memory.
+bool decode_eligible(qmc_model *m, DevCtx *c) {
+    if (m->tp != 1 || m->hd > 128) return false;
+    auto q = [](int dt) { return dt == QMC_Q8_0 || dt == QMC_Q4_0; };
+    if (!q(m->dt_out)) return false;
+    int64_t umax = split_row_bytes(m->dt_out, m->D);
+    int nbmax = (int)nblocks(m->D);
+    for (const Layer &l : m->layers) {
+        if (!q(l.dt[QMC_T_WQ]) || !q(l.dt[QMC_T_WO]) || !q(l.dt[QMC_T_W1]) || !q(l.dt[QMC_T_W2])) return false;
+        umax = std::max(umax, 2 * split_row_bytes(l.dt[QMC_T_WQ], m->D));
+        umax = std::max(umax, 2 * split_row_bytes(l.dt[QMC_T_W1], m->D));
+        umax = std::max(umax, split_row_bytes(l.dt[QMC_T_WO], m->Dl));
+        umax = std::max(umax, split_row_bytes(l.dt[QMC_T_W2], m->Hl));
+    }
+    nbmax = std::max(nbmax, (int)std::max(nblocks(m->Dl), nblocks(m->Hl)));
+    return plan_decode(umax, nbmax, m->hd, m->NH / m->NKV, c->max_smem_optin, &m->plan);
+}
+
+// split-row copies of every matrix (allocated once, refilled after any upload); FFN rows interleaved
+// w1[0], w3[0], w1[1], ... so one copy streams both rows of a SwiGLU unit
+int repack_weights(qmc_model *m) {
+    cudaStream_t s = m->stream;
+    for (Layer &l : m->layers) {
+        const int dq = l.dt[QMC_T_WQ], dw = l.dt[QMC_T_WO], d1 = l.dt[QMC_T_W1], d2 = l.dt[QMC_T_W2];
+        const int64_t rq = split_row_bytes(dq, m->D), ro = split_row_bytes(dw, m->Dl), r1 = split_row_bytes(d1, m->D),
+                      r2 = split_row_bytes(d2, m->Hl);
+        const int64_t nq = m->Dl + 2 * m->KVl;
+        if (!l.sqkv && (dalloc(m, (void **)&l.sqkv, (size_t)(nq * rq)) || dalloc(m, (void **)&l.swo, (size_t)(m->D * ro)) ||
+                        dalloc(m, (void **)&l.s13, (size_t)(2 * m->Hl * r1)) || dalloc(m, (void **)&l.sw2, (size_t)(m->D * r2))))
+            return QMC_ENOMEM;
+        RC(launch_repack_split(dq, l.wqkv, nq, m->D, l.sqkv, rq, s));
+        RC(launch_repack_split(dw, l.wo, m->D, m->Dl, l.swo, ro, s));
+        RC(launch_repack_split(d1, l.w1, m->Hl, m->D, l.s13, 2 * r1, s));
+        RC(launch_repack_split(d1, l.w3, m->Hl, m->D, l.s13 + r1, 2 * r1, s));
+        RC(launch_repack_split(d2, l.w2, m->D, m->Hl, l.sw2, r2, s));
+    }
+    const int64_t rout = split_row_bytes(m->dt_out, m->D);
+    if (!m->sout && dalloc(m, (void **)&m->sout, (size_t)(m->Vl * rout))) return QMC_ENOMEM;
+    RC(launch_repack_split(m->dt_out, m->out, m->Vl, m->D, m->sout, rout, s));
+    QMC_CUDA(cudaStreamSynchronize(s));
+    m->repacked = true;
+    return QMC_OK;
+}
+
+DecodePhase matrix_phase(const qmc_model *m, int kind, int dt, const uint8_t *W, int64_t units, int64_t K, int urows,
+                         const float *in, const float *norm_w, float *out) {
+    DecodePhase ph{};
+    ph.kind = kind;
+    ph.dtype = dt;
+    ph.W = W;
+    ph.units = units;
+    ph.K = (int)K;
+    ph.nb = (int)nblocks(K);
+    ph.urows = urows;
+    ph.rbytes = (int)split_row_bytes(dt, K);
+    ph.sbytes = (int)split_scale_bytes(K);
+    ph.R = std::max(1, (int)(m->plan.slot_bytes / ((int64_t)urows * ph.rbytes)));
+    ph.in = in;
+    ph.norm_w = norm_w;
+    ph.out = out;
+    return ph;
+}
+
+int prepare_decode(qmc_model *m, DevCtx *c) {
+    if (!m->mega_checked) {
+        m->mega_checked = true;
+        m->mega = decode_eligible(m, c);
+        if (!m->mega) return QMC_OK;
+        RC(repack_weights(m));  // allocates the split-row copies the phase list points at
+        const int64_t kvstride = (int64_t)m->S * m->KVl;
+        for (int l = 0; l < m->L; l++) {
+            Layer &Ly = m->layers[l];
+            float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
+            DecodePhase qkv = matrix_phase(m, PH_QKV, Ly.dt[QMC_T_WQ], Ly.sqkv, (m->Dl + 2 * m->KVl) / 2, m->D, 2, m->x,
+                                           Ly.attn_norm, nullptr);
+            qkv.embed = l == 0;
+            qkv.kc = kcl, qkv.vc = vcl;
+            DecodePhase at{};
+            at.kind = PH_ATTN;
+            at.kc = kcl, at.vc = vcl;
+            m->phases.push_back(qkv);
+            m->phases.push_back(at);
+            m->phases.push_back(matrix_phase(m, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x));
+            m->phases.push_back(matrix_phase(m, PH_FFN, Ly.dt[QMC_T_W1], Ly.s13, m->Hl, m->D, 2, m->x, Ly.ffn_norm, m->h));
+            m->phases.push_back(matrix_phase(m, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x));
+        }
+        m->phases.push_back(matrix_phase(m, PH_OUT, m->dt_out, m->sout, m->Vl, m->D, 1, m->x, m->norm, m->logits));
+        const int group = m->NH / m->NKV;
+        m->gsplit = (group + kDecodeHeadsPerUnit - 1) / kDecodeHeadsPerUnit;
+        m->maxseg = std::max(1, c->num_sms / (m->NKVl * m->gsplit));
+        const size_t units = (size_t)m->NKVl * m->gsplit;
+        RC(dalloc(m, (void **)&m->d_phases, m->phases.size() * sizeof(DecodePhase)));
+        RC(dalloc(m, (void **)&m->gbar, 64));
+        RC(dalloc(m, (void **)&m->apart, units * m->maxseg * kDecodeHeadsPerUnit * (m->hd + 2) * 4));
+        RC(dalloc(m, (void **)&m->acnt, units * 4));
+        QMC_CUDA(cudaMemcpy(m->d_phases, m->phases.data(), m->phases.size() * sizeof(DecodePhase), cudaMemcpyHostToDevice));
+        QMC_CUDA(cudaMemset(m->gbar, 0, 64));
+        QMC_CUDA(cudaMemset(m->acnt, 0, units * 4));
+        return QMC_OK;
+    }
+    if (m->mega && !m->repacked) RC(repack_weights(m));
+    return QMC_OK;
+}
+
+int launch_decode_step(qmc_model *m, DevCtx *c) {
+    DecodeParams p{};
+    p.ph = m->d_phases;
+    p.nph = (int)m->phases.size();
+    p.D = m->D, p.Dq = m->Dl, p.KVl = m->KVl, p.hd = m->hd, p.nkv = m->NKVl, p.group = m->NH / m->NKV;
+    p.gsplit = m->gsplit;
+    p.eps = m->cfg.norm_eps;
+    p.scale = 1.0f / sqrtf((float)m->hd);
+    p.tok = m->tok;
+    p.dt_tok = m->dt_tok;
+    p.x = m->x, p.q = m->q, p.xb = m->xb;
+    p.rope = m->rope;
+    p.state = m->state, p.forced = m->forced, p.gen = m->gen, p.gen_cap = m->S;
+    p.vocab = m->V;
+    p.amax_key = m->amax;
+    p.amax_ctr = (int *)(m->amax + 1);
+    p.gbar = m->gbar;
+    p.apart = m->apart, p.acnt = m->acnt, p.maxseg = m->maxseg;
+    p.err = c->err;
+    p.nslots = m->plan.nslots, p.slot_bytes = m->plan.slot_bytes;
+    p.off_bars = m->plan.off_bars, p.off_xq = m->plan.off_xq, p.off_xds = m->plan.off_xds, p.off_red = m->plan.off_red;
+    return launch_decode(p, m->plan, c->num_sms, m->stream);
+}
+
+// after a device-side timeout the barrier words and tickets may be mid-count: clear them
+int step_status(qmc_model *m) {
+    const int rc = qmc_check_device_error();
+    if (rc && m->mega) {
+        cudaMemset(m->gbar, 0, 64);
+        cudaMemset(m->acnt, 0, (size_t)m->NKVl * m->gsplit * 4);
+        cudaMemset(m->amax, 0, 16);
+    }
+    return rc;
+}
+
 // enqueue one decode step on m->stream (captured into the graph)
 int enqueue_step(qmc_model *m) {
     cudaStream_t s = m->stream;
     DevCtx *c = ctx();
+    if (m->mega) return launch_decode_step(m, c);
     const int *pos = m->state + 1;
     RC(launch_embed(m->dt_tok, m->tok, m->D, m->state, m->x, s, true));
     const int64_t kvstride = (int64_t)m->S * m->KVl;
@@ -287,8 +441,9 @@ int enqueue_step(qmc_model *m) {
 }
 
 int build_graph(qmc_model *m) {
-    if (m->graph) return QMC_OK;
+    if (m->graph) return m->mega && !m->repacked ? repack_weights(m) : QMC_OK;
     if (!complete(m)) return set_error(QMC_ESTATE, "model: not every tensor has been uploaded");
+    RC(prepare_decode(m, ctx()));
     cudaGraph_t g = nullptr;
     QMC_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int rc = enqueue_step(m);
@@ -412,8 +567,7 @@ int qmc_model_upload(qmc_model *m, int kind, int layer, int dtype, int64_t rows,
         QMC_CUDA(cudaMemcpy2D(dst, (size_t)rbl, src + off, (size_t)rb, (size_t)rbl, (size_t)s.nr, cudaMemcpyHostToDevice));
     }
     mark(m, kind, layer, dtype);
-    if (m->graph) {  // a re-upload keeps the graph valid (same buffers)
-    }
+    m->repacked = false;  // split-row copies are refilled before the next step
     return QMC_OK;
 }
 
@@ -442,6 +596,7 @@ int qmc_model_synthesize(qmc_model *m, int dtype, uint64_t seed, double stdv) {
         else RC(launch_synth(seed, (uint64_t)t, dt, s.cols, s.r0, s.nr, s.c0, s.nc, stdv, dst, m->stream));
         mark(m, kind, layer, dt);
     }
+    m->repacked = false;
     QMC_CUDA(cudaStreamSynchronize(m->stream));
     return QMC_OK;
 }
@@ -458,7 +613,7 @@ int qmc_model_forward(qmc_model *m, int32_t token, int32_t pos, float *logits_ho
     if (logits_host) QMC_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, m->stream));
     QMC_CUDA(cudaMemcpyAsync(m->h_state + 4, m->state, 4, cudaMemcpyDeviceToHost, m->stream));
     QMC_CUDA(cudaStreamSynchronize(m->stream));
-    RC(qmc_check_device_error());
+    RC(step_status(m));
     if (logits_host) memcpy(logits_host, m->h_logits, (size_t)m->V * 4);
     if (next_token) *next_token = m->h_state[4];
     return QMC_OK;
@@ -480,7 +635,7 @@ int qmc_model_generate(qmc_model *m, const int32_t *prompt, int32_t n_prompt, in
     for (int i = 0; i < steps; i++) QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
     QMC_CUDA(cudaMemcpyAsync(out_tokens, m->gen, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, m->stream));
     QMC_CUDA(cudaStreamSynchronize(m->stream));
-    return qmc_check_device_error();
+    return step_status(m);
 }
 
 int qmc_model_enqueue_decode(qmc_model *m, int32_t token, int32_t pos, int32_t steps) {
@@ -504,7 +659,7 @@ int qmc_model_state(qmc_model *m, int32_t *token, int32_t *pos) {
     QMC_CUDA(cudaStreamSynchronize(m->stream));
     if (token) *token = m->h_state[12];
     if (pos) *pos = m->h_state[13];
-    return qmc_check_device_error();
+    return step_status(m);
 }
 
 int qmc_model_logits(qmc_model *m, const float **dev_logits) {
