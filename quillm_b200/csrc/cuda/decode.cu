@@ -26,8 +26,9 @@
 // src/quant.c:33-53) after the fused rmsnorm (src/ops.c:93-98).
 //
 // Attention (src/model.c:132-156): (KV head, position segment) units over the CTAs; the 12 warps of a
-// CTA walk the segment's positions with an online softmax per query head, merge in shared memory, and
-// the last CTA of a head (ticket) merges the segments' (max, sum, acc) partials into the head's output.
+// CTA walk the segment's positions with an online softmax per query head and merge in shared memory;
+// each segment's (max, sum, acc) partial goes to global memory and the wo phase's prologue merges the
+// segments of a head while it quantizes the attention output (no extra barrier or ticket).
 //
 // Every wait is bounded (mbarrier waits, the grid barrier): on expiry a thread raises the error word and
 // continues without waiting, so the launch always ends; the host then reports QMC_ETIMEOUT.
@@ -49,11 +50,16 @@ constexpr int XW = 4;               // activation blocks per lane kept in regist
 constexpr int GMAX = kDecodeHeadsPerUnit;  // query heads per attention unit (a larger GQA group spans units)
 constexpr int MAXW = 4;             // head_dim / 32 (head_dim <= 128)
 constexpr int kMinAttnPos = 32;     // an attention segment spans at least this many positions
+constexpr int kAttnChunk = 4;       // positions per warp whose K/V rows are loaded together
+constexpr int kPartHead = kDecodePartHead;  // partial: (max, sum, 2 pad, acc[hd]), acc 16-byte aligned
+constexpr int kFastSegs = 4;        // segment partials the wo prologue merges with all loads in flight
 // named barriers: 0 = __syncthreads, 1..NG = the groups, kBarConsumers = all consumer warps
 constexpr int kBarConsumers = NG + 1;
 // shared scratch at off_red: prologue partial sums, argmax keys, grid-barrier flag
 constexpr int kRedDred = 0, kRedKeys = 128;
-constexpr int kRedFlag = kRedKeys + NCW * 8, kRedBytes = kRedFlag + 128;
+constexpr int kRedFlag = kRedKeys + NCW * 8, kRedDesc = kRedFlag + 128;
+constexpr int kRedBytes = kRedDesc + 2 * (int)sizeof(DecodePhase);  // + this and the next phase's descriptor
+static_assert(sizeof(DecodePhase) % 16 == 0, "descriptors are copied in 16-byte chunks");
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -78,7 +84,7 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsi
 
 // ---------------------------------------------------------------- grid barrier (consumer threads)
 // One monotonic arrival counter per step: barrier j is passed once (j + 1) * gridDim.x arrivals are seen.
-// Thread 0 arrives with a release atomic after a CTA barrier (so the CTA's epilogue stores are ordered
+// Thread 0 arrives with a release reduction after a CTA barrier (so the CTA's epilogue stores are ordered
 // before it) and polls with acquire loads (bounded); the step's last CTA resets the counter for the next
 // launch.  Activations written before a barrier are read after it with L2 (.cg) loads.
 __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
@@ -105,6 +111,19 @@ __device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, b
     return *flag != 0;
 }
 
+// ---------------------------------------------------------------- phase descriptors in shared memory
+// The consumers read the current phase's descriptor from shared memory: the next one is copied there
+// asynchronously (cp.async) while the current phase runs, so a phase start costs no global round trip.
+__device__ __forceinline__ void desc_prefetch(const DecodePhase *src, DecodePhase *dst) {
+    const int t = threadIdx.x;
+    if (t < (int)(sizeof(DecodePhase) / 16))
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32((uint8_t *)dst + 16 * t)),
+                     "l"((const uint8_t *)src + 16 * t)
+                     : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void desc_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---------------------------------------------------------------- producer
 __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uint64_t *empty) {
     unsigned gk = 0;
@@ -128,10 +147,86 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
 }
 
 // ---------------------------------------------------------------- prologue: input -> Q8_0 activations
+// number of position segments the attention phase splits each head into at position pos
+__device__ __forceinline__ int attn_segments(const DecodeParams &p, int pos) {
+    return max(1, min(p.maxseg, (pos + kMinAttnPos) / kMinAttnPos));
+}
+
+// segment partial (max, sum, 2 pad, acc[hd]) of query head hq
+__device__ __forceinline__ const float *attn_part(const DecodeParams &p, int hq, int seg) {
+    const int kvh = hq / p.group, r = hq % p.group, unit = kvh * p.gsplit + r / GMAX, g = r % GMAX;
+    return p.apart + (((int64_t)unit * p.maxseg + seg) * GMAX + g) * (p.hd + kPartHead);
+}
+
+// 16 consecutive elements of the attention output, merged from the head's segment partials
+// (src/model.c:141-153): out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s, M the largest m_s
+__device__ void attn_out16(const DecodeParams &p, int64_t e0, int K, int nseg, float (&v)[16]) {
+    const int hd = p.hd;
+    if ((hd & 15) == 0 && e0 + 16 <= K && nseg <= kFastSegs) {  // one head, few segments: loads at once
+        const int hq = (int)(e0 / hd), d0 = (int)(e0 % hd);
+        const float *head = attn_part(p, hq, 0), *src = head + kPartHead + d0;  // segment 0: (max, sum), acc
+        const int64_t sstride = (int64_t)GMAX * (hd + kPartHead);
+        float2 ml[kFastSegs];
+        float4 o[kFastSegs][4];
+#pragma unroll
+        for (int sg = 0; sg < kFastSegs; sg++) {
+            const bool ok = sg < nseg;
+            ml[sg] = ok ? __ldcg((const float2 *)(head + sg * sstride)) : make_float2(-INFINITY, 0.0f);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                o[sg][i] = ok ? __ldcg((const float4 *)(src + sg * sstride) + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int sg = 0; sg < kFastSegs; sg++) M = ml[sg].y > 0.0f ? fmaxf(M, ml[sg].x) : M;
+        float den = 0.0f, num[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) num[i] = 0.0f;
+#pragma unroll
+        for (int sg = 0; sg < kFastSegs; sg++) {
+            const float c = ml[sg].y > 0.0f ? expf(ml[sg].x - M) : 0.0f;
+            den = fmaf(c, ml[sg].y, den);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                num[4 * i] = fmaf(c, o[sg][i].x, num[4 * i]);
+                num[4 * i + 1] = fmaf(c, o[sg][i].y, num[4 * i + 1]);
+                num[4 * i + 2] = fmaf(c, o[sg][i].z, num[4 * i + 2]);
+                num[4 * i + 3] = fmaf(c, o[sg][i].w, num[4 * i + 3]);
+            }
+        }
+        const float rden = 1.0f / den;
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = num[i] * rden;
+        return;
+    }
+    for (int i = 0; i < 16; i++) {  // generic: element by element
+        const int64_t e = e0 + i;
+        if (e >= K) {
+            v[i] = 0.0f;
+            continue;
+        }
+        const int hq = (int)(e / hd), d = (int)(e % hd);
+        float M = -INFINITY, den = 0.0f, num = 0.0f;
+        for (int sg = 0; sg < nseg; sg++) {
+            const float *src = attn_part(p, hq, sg);
+            const float m = __ldcg(src), l = __ldcg(src + 1), o = __ldcg(src + kPartHead + d);
+            if (l > 0.0f) {
+                const float Mn = fmaxf(M, m);
+                const float c0 = den > 0.0f ? expf(M - Mn) : 0.0f, c1 = expf(m - Mn);
+                den = fmaf(den, c0, c1 * l);
+                num = fmaf(num, c0, c1 * o);
+                M = Mn;
+            }
+        }
+        v[i] = num / den;
+    }
+}
+
 // 16 elements e0..e0+15 of the phase input: the token's embedding row (dequantized as src/quant.c:65-94,
-// one rounding) for the first phase, else the input vector; zero past K
+// one rounding) for the first phase, the merged attention output for wo, else the input vector; zero
+// past K
 __device__ __forceinline__ void fetch16(const DecodeParams &p, const DecodePhase &ph, const uint8_t *erow, int64_t e0,
-                                        float (&v)[16]) {
+                                        int nseg, float (&v)[16]) {
     const int K = ph.K;
     if (e0 >= K) {  // pairs past the last block (their block and its scale lie outside the row)
 #pragma unroll
@@ -158,6 +253,10 @@ __device__ __forceinline__ void fetch16(const DecodeParams &p, const DecodePhase
                 v[i] = e0 + i < K ? d * (float)(((k & 1) ? (byte >> 4) : (byte & 15)) - 8) : 0.0f;
             }
         }
+        return;
+    }
+    if (ph.kind == PH_WO) {
+        attn_out16(p, e0, K, nseg, v);
         return;
     }
     const float *src = ph.in + e0;
@@ -189,6 +288,12 @@ __device__ __forceinline__ void fetch16_w(const float *w, int64_t e0, int K, flo
 // loading consecutive blocks hit all 32 banks
 __device__ __forceinline__ int xswz(int b) { return ((b >> 2) & 1) << 4; }
 
+// x + kRound - kRound rounds |x| < 2^22 to the nearest integer, ties to even, in one round-to-nearest
+// add; for |x| <= 127 the integer is also the low bits of x + kRound.  Used instead of rintf / floorf /
+// float->int conversions, which issue at a fraction of the FMA pipe's rate.
+constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+constexpr int kRoundBits = 0x4B400000;
+
 // Quotients v / sc for the quantizer (src/quant.c:47-50 divides, then rounds half to even).  |v / sc| <
 // 256, so r = v * (1 / sc) lies within 4.6e-5 of the correctly rounded quotient and rounds to the same
 // integer unless that quotient is within 4.6e-5 of a half-integer.  If any of the lane's 16 products is
@@ -200,7 +305,8 @@ __device__ __forceinline__ void quotients16(const float (&v)[16], float sc, floa
 #pragma unroll
     for (int i = 0; i < 16; i++) {
         r[i] = __fmul_rn(v[i], rs);
-        near |= fabsf(__fsub_rn(r[i], floorf(r[i])) - 0.5f) < 1.0e-4f;
+        const float n = __fsub_rn(__fadd_rn(r[i], kRound), kRound);  // nearest integer
+        near |= fabsf(__fsub_rn(r[i], n)) > 0.4999f;
     }
     if (near) {
 #pragma unroll
@@ -209,42 +315,47 @@ __device__ __forceinline__ void quotients16(const float (&v)[16], float sc, floa
 }
 
 // Q8_0 of block b held by a lane pair (part j: elements 16j..16j+15), bit-exact with src/quant.c:33-53:
-// amax ignores NaN, IEEE division for the scale, fp16 RNE scale, then the quantized elements.  All lanes
-// call it (pair shuffles); `active` lanes store.  Q4_0 weights take the block's even elements in bytes
-// 0-15 and odd elements in bytes 16-31.
+// amax ignores NaN, IEEE division for the scale, fp16 RNE scale, then rint(v / scale) clamped to +-127
+// (NaN -> 0, as the float->int conversion gives).  All lanes call it (pair shuffles); `active` lanes
+// store.  Q4_0 weights take the block's even elements in bytes 0-15 and odd elements in bytes 16-31.
 __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int b, int j, bool active,
                                             const float (&v)[16]) {
-    uint32_t ab = 0;
+    uint32_t m[8];
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-        const float a = fabsf(v[i]);
-        ab = max(ab, (a == a) ? __float_as_uint(a) : 0u);  // |v| bits order like floats; NaN -> 0
+    for (int i = 0; i < 8; i++) {  // |v| bits order like floats; NaN -> 0
+        const float a0 = fabsf(v[2 * i]), a1 = fabsf(v[2 * i + 1]);
+        m[i] = max((a0 == a0) ? __float_as_uint(a0) : 0u, (a1 == a1) ? __float_as_uint(a1) : 0u);
     }
-    ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 1));
+#pragma unroll
+    for (int w = 4; w; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; i++) m[i] = max(m[i], m[i + w]);
+    const uint32_t ab = max(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
     const float sc = h2f(f2h(__fdiv_rn(__uint_as_float(ab), 127.0f)));
     float qf[16];
     quotients16(v, sc, qf);
-    uint32_t w[4] = {0u, 0u, 0u, 0u};  // Q8_0: bytes 16j.. in order; Q4_0: even | odd elements
-    int sum = 0;
+    int q[16];
 #pragma unroll
     for (int i = 0; i < 16; i++) {
-        float rq = rintf(qf[i]);
-        rq = rq < -127.0f ? -127.0f : rq;
-        rq = rq > 127.0f ? 127.0f : rq;
-        const int q = sc != 0.0f ? (int)rq : 0;
-        sum += q;
-        const int k = q4 ? ((i & 1) ? 8 : 0) + (i >> 1) : i;  // byte index within this lane's 16
-        w[k >> 2] |= (uint32_t)(q & 0xff) << (8 * (k & 3));
+        const float c = fminf(fmaxf(qf[i], -127.0f), 127.0f);
+        q[i] = (sc != 0.0f && qf[i] == qf[i]) ? __float_as_int(__fadd_rn(c, kRound)) - kRoundBits : 0;
     }
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) sum += (q[i] + q[i + 1]) + (q[i + 2] + q[i + 3]);
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     if (!active) return;
+    auto pk = [&](int a, int b2, int c, int d) {
+        return (uint32_t)(q[a] & 0xff) | ((uint32_t)(q[b2] & 0xff) << 8) | ((uint32_t)(q[c] & 0xff) << 16) |
+               ((uint32_t)q[d] << 24);
+    };
     uint8_t *blk = xq + (int64_t)b * 32;
     const int sw = xswz(b);
     if (!q4) {
-        *(uint4 *)(blk + ((16 * j) ^ sw)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *(uint4 *)(blk + ((16 * j) ^ sw)) = make_uint4(pk(0, 1, 2, 3), pk(4, 5, 6, 7), pk(8, 9, 10, 11), pk(12, 13, 14, 15));
     } else {
-        *(uint2 *)(blk + ((8 * j) ^ sw)) = make_uint2(w[0], w[1]);
-        *(uint2 *)(blk + ((16 + 8 * j) ^ sw)) = make_uint2(w[2], w[3]);
+        *(uint2 *)(blk + ((8 * j) ^ sw)) = make_uint2(pk(0, 2, 4, 6), pk(8, 10, 12, 14));
+        *(uint2 *)(blk + ((16 + 8 * j) ^ sw)) = make_uint2(pk(1, 3, 5, 7), pk(9, 11, 13, 15));
     }
     if (j == 0) xds[b] = make_int2(__float_as_int(sc), sum);
 }
@@ -252,7 +363,7 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
 // The phase input (optionally x * inv * w, inv = (float)(1 / sqrt(sum_double(x^2)/n + eps)),
 // src/ops.c:93-98) quantized into shared memory by the consumer threads, two per block; the first
 // phase's CTA 0 also stores the embedding into x.  The first round's x and w stay in registers.
-__device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int token) {
+__device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int token, int pos) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, qd = t >> 1, j = t & 1;
     uint8_t *xq = sm + p.off_xq;
     int2 *xds = (int2 *)(sm + p.off_xds);
@@ -261,9 +372,10 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
     const uint8_t *erow = ph.embed ? p.tok + (int64_t)token * row_bytes(p.dt_tok, K) : nullptr;
     const bool keep_x = ph.embed && blockIdx.x == 0;
     const float *nw = ph.norm_w;
+    const int nseg = attn_segments(p, pos);
     const int64_t e00 = (int64_t)qd * 32 + 16 * j;
     float v0[16], w0[16];
-    fetch16(p, ph, erow, e00, v0);
+    fetch16(p, ph, erow, e00, nseg, v0);
     if (nw) fetch16_w(nw, e00, K, w0);
     float inv = 1.0f;
     if (nw) {
@@ -272,7 +384,7 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
         for (int i = 0; i < 16; i++) ss = fma((double)v0[i], (double)v0[i], ss);
         for (int r = 1; r < rounds; r++) {
             float v[16];
-            fetch16(p, ph, erow, (int64_t)(r * QPR + qd) * 32 + 16 * j, v);
+            fetch16(p, ph, erow, (int64_t)(r * QPR + qd) * 32 + 16 * j, nseg, v);
 #pragma unroll
             for (int i = 0; i < 16; i++) ss = fma((double)v[i], (double)v[i], ss);
         }
@@ -287,6 +399,7 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
     }
     float v1[16], w1[16];
     for (int r = 0; r < rounds; r++) {
+        if (r * QPR + warp * 16 >= ph.nb) break;  // this warp's blocks (and later rounds') are past the row
         const int b = r * QPR + qd;
         const int64_t e0 = (int64_t)b * 32 + 16 * j;
         if (r > 0) {
@@ -295,7 +408,7 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
         }
         if (r + 1 < rounds) {  // next round's loads in flight while this one is quantized
             const int64_t e1 = e0 + (int64_t)QPR * 32;
-            fetch16(p, ph, erow, e1, v1);
+            fetch16(p, ph, erow, e1, nseg, v1);
             if (nw) fetch16_w(nw, e1, K, w1);
         }
         if (keep_x) {
@@ -360,7 +473,7 @@ __device__ __forceinline__ void rope_pair(float a, float b, float2 cs, float &o0
     o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
 }
 
-// operand an epilogue lane needs besides the row sums, loaded before the unit.s dots so its latency is
+// operand an epilogue lane needs besides the row sums, loaded before the unit's dots so its latency is
 // hidden: the RoPE (cos, sin) of a q/k pair, or the residual value of x
 __device__ __forceinline__ float2 epilogue_operand(const DecodeParams &p, const DecodePhase &ph, int64_t unit, int pos) {
     if (ph.kind == PH_QKV) {
@@ -499,12 +612,11 @@ __device__ void run_matvec(const DecodeParams &p, const DecodePhase &ph, uint8_t
 __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int pos) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int npos = pos + 1, nunit = p.nkv * p.gsplit;
-    int nseg = min(p.maxseg, (npos + kMinAttnPos - 1) / kMinAttnPos);
-    if (nseg < 1) nseg = 1;
+    const int nseg = attn_segments(p, pos);
     const bool active = (int)blockIdx.x < nunit * nseg;
     const int unit = active ? (int)blockIdx.x / nseg : 0, seg = active ? (int)blockIdx.x % nseg : 0;
     const int kvh = unit / p.gsplit, gs = unit % p.gsplit, h0 = gs * GMAX, G = min(GMAX, p.group - h0);
-    const int hd = p.hd, stride = hd + 2;
+    const int hd = p.hd, stride = hd + 2, ps = hd + kPartHead;
     const int chunk = (npos + nseg - 1) / nseg, t0 = seg * chunk, t1 = active ? min(npos, t0 + chunk) : 0;
     const int64_t hq = (int64_t)kvh * p.group + h0;  // first query head of this unit
     const float *kb = ph.kc + (int64_t)kvh * hd, *vb = ph.vc + (int64_t)kvh * hd;
@@ -521,39 +633,36 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
             o[g][w] = 0.0f;
         }
     }
-    // positions t0 + warp, + 12, ...; the next position's K and V rows are loaded before this one is used
-    float kn[MAXW], vn[MAXW];
-    int tt = t0 + warp;
+    // positions t0 + warp, + 12, ...: the K and V rows of up to kAttnChunk of them are loaded at once
+    for (int tb = t0 + warp; tb < t1; tb += kAttnChunk * NCW) {
+        float k[kAttnChunk][MAXW], v[kAttnChunk][MAXW];
 #pragma unroll
-    for (int w = 0; w < MAXW; w++) {
-        const int d = lane + 32 * w;
-        kn[w] = (tt < t1 && d < hd) ? __ldcg(kb + (int64_t)tt * p.KVl + d) : 0.0f;
-        vn[w] = (tt < t1 && d < hd) ? __ldcg(vb + (int64_t)tt * p.KVl + d) : 0.0f;
-    }
-    for (; tt < t1; tt += NCW) {
-        float k[MAXW], v[MAXW];
+        for (int c = 0; c < kAttnChunk; c++) {
+            const int tt = tb + c * NCW;
 #pragma unroll
-        for (int w = 0; w < MAXW; w++) k[w] = kn[w], v[w] = vn[w];
-        const int tn = tt + NCW;
-#pragma unroll
-        for (int w = 0; w < MAXW; w++) {
-            const int d = lane + 32 * w;
-            kn[w] = (tn < t1 && d < hd) ? __ldcg(kb + (int64_t)tn * p.KVl + d) : 0.0f;
-            vn[w] = (tn < t1 && d < hd) ? __ldcg(vb + (int64_t)tn * p.KVl + d) : 0.0f;
+            for (int w = 0; w < MAXW; w++) {
+                const int d = lane + 32 * w;
+                k[c][w] = (tt < t1 && d < hd) ? __ldcg(kb + (int64_t)tt * p.KVl + d) : 0.0f;
+                v[c][w] = (tt < t1 && d < hd) ? __ldcg(vb + (int64_t)tt * p.KVl + d) : 0.0f;
+            }
         }
 #pragma unroll
-        for (int g = 0; g < GMAX; g++) {
-            if (g < G) {
-                float s = 0.0f;
+        for (int c = 0; c < kAttnChunk; c++) {
+            if (tb + c * NCW >= t1) break;
 #pragma unroll
-                for (int w = 0; w < MAXW; w++) s = fmaf(k[w], q[g][w], s);
-                s = warp_sum(s) * p.scale;
-                const float mn = fmaxf(m[g], s);
-                const float corr = expf(m[g] - mn), e = expf(s - mn);
-                l[g] = l[g] * corr + e;
+            for (int g = 0; g < GMAX; g++) {
+                if (g < G) {
+                    float sc = 0.0f;
 #pragma unroll
-                for (int w = 0; w < MAXW; w++) o[g][w] = o[g][w] * corr + e * v[w];
-                m[g] = mn;
+                    for (int w = 0; w < MAXW; w++) sc = fmaf(k[c][w], q[g][w], sc);
+                    sc = warp_sum(sc) * p.scale;
+                    const float mn = fmaxf(m[g], sc);
+                    const float corr = expf(m[g] - mn), e = expf(sc - mn);
+                    l[g] = l[g] * corr + e;
+#pragma unroll
+                    for (int w = 0; w < MAXW; w++) o[g][w] = o[g][w] * corr + e * v[c][w];
+                    m[g] = mn;
+                }
             }
         }
     }
@@ -593,56 +702,23 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
         n = h;
     }
     if (!active || warp != 0) return;
-    if (nseg == 1) {
-#pragma unroll
-        for (int g = 0; g < GMAX; g++)
-            if (g < G)
-#pragma unroll
-                for (int w = 0; w < MAXW; w++)
-                    if (lane + 32 * w < hd) __stcg(p.xb + (hq + g) * hd + lane + 32 * w, o[g][w] / l[g]);
-        return;
-    }
-    // segment partial -> global; the last segment of this unit merges them (src/model.c:141-153)
-    float *part = p.apart + ((int64_t)unit * p.maxseg + seg) * GMAX * stride;
+    // this segment's (max, sum, acc) per query head -> global; the wo phase's prologue merges the
+    // segments of each head while it quantizes the attention output (src/model.c:141-153)
+    float *part = p.apart + ((int64_t)unit * p.maxseg + seg) * GMAX * ps;
 #pragma unroll
     for (int g = 0; g < GMAX; g++) {
         if (g < G) {
-            if (lane == 0) __stcg(part + g * stride, m[g]), __stcg(part + g * stride + 1, l[g]);
+            float *dst = part + g * ps;
+            if (lane == 0) __stcg(dst, m[g]), __stcg(dst + 1, l[g]);
 #pragma unroll
             for (int w = 0; w < MAXW; w++)
-                if (lane + 32 * w < hd) __stcg(part + g * stride + 2 + lane + 32 * w, o[g][w]);
+                if (lane + 32 * w < hd) __stcg(dst + kPartHead + lane + 32 * w, o[g][w]);
         }
     }
-    __threadfence();
-    int tk = 0;
-    if (lane == 0) tk = atomicAdd(p.acnt + unit, 1);
-    tk = __shfl_sync(0xffffffffu, tk, 0);
-    if (tk != nseg - 1) return;
-    __threadfence();
-    const float *base = p.apart + (int64_t)unit * p.maxseg * GMAX * stride;
-    for (int g = 0; g < G; g++) {
-        float M = -INFINITY;
-        for (int sg = 0; sg < nseg; sg++) M = fmaxf(M, __ldcg(base + (sg * GMAX + g) * stride));
-#pragma unroll
-        for (int w = 0; w < MAXW; w++) {
-            const int d = lane + 32 * w;
-            if (d >= hd) continue;
-            float num = 0.0f, den = 0.0f;
-            for (int sg = 0; sg < nseg; sg++) {
-                const float *src = base + (sg * GMAX + g) * stride;
-                const float ls = __ldcg(src + 1);
-                const float c = ls > 0.0f ? expf(__ldcg(src) - M) : 0.0f;
-                den = fmaf(c, ls, den);
-                num = fmaf(c, __ldcg(src + 2 + d), num);
-            }
-            __stcg(p.xb + (hq + g) * hd + d, num / den);
-        }
-    }
-    if (lane == 0) atomicExch(p.acnt + unit, 0);
 }
 
 // ---------------------------------------------------------------- greedy argmax over the logits
-__device__ void logits_argmax(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, unsigned long long best) {
+__device__ void logits_argmax(const DecodeParams &p, uint8_t *sm, unsigned long long best) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     unsigned long long *keys = (unsigned long long *)(sm + p.off_red + kRedKeys);
 #pragma unroll
@@ -658,7 +734,7 @@ __device__ void logits_argmax(const DecodeParams &p, const DecodePhase &ph, uint
             __threadfence();
             const unsigned long long gmax = atomicExch(p.amax_key, 0ull);
             int bi = argmax_index(gmax);
-            const float x0 = __ldcg(ph.out);
+            const float x0 = __ldcg(p.logits);
             if (x0 != x0) bi = 0;  // a NaN in slot 0 is never replaced by the reference (src/sampler.c:27-32)
             advance_state(bi, p.state, p.forced, p.gen, p.gen_cap);
             *p.amax_ctr = 0;
@@ -694,14 +770,22 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
     unsigned gk = 0;
     bool dead = false;
     unsigned long long best = 0;
+    DecodePhase *dsm = (DecodePhase *)(sm + p.off_red + kRedDesc);
+    desc_prefetch(p.ph, dsm);
+    desc_wait();
+    named_sync(kBarConsumers, NCT);
     for (int i = 0; i < p.nph; i++) {
-        const DecodePhase &ph = p.ph[i];
-        if (i > 0 && !grid_sync(p, sm, (unsigned)i * gridDim.x, dead)) dead = true;
+        if (i > 0) {
+            desc_wait();  // phase i's descriptor (copied during phase i - 1); the barrier publishes it
+            if (!grid_sync(p, sm, (unsigned)i * gridDim.x, dead)) dead = true;
+        }
+        const DecodePhase &ph = dsm[i & 1];
+        if (i + 1 < p.nph) desc_prefetch(p.ph + i + 1, dsm + ((i + 1) & 1));
         if (ph.kind == PH_ATTN) {
             attention(p, ph, sm, pos);
             continue;
         }
-        prologue(p, ph, sm, token);
+        prologue(p, ph, sm, token, pos);
         const bool two = ph.urows == 2;
         if (ph.dtype == QMC_Q8_0) {
             if (two) run_matvec<QMC_Q8_0, true>(p, ph, sm, full, empty, gk, dead, pos, best);
@@ -710,7 +794,7 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
             if (two) run_matvec<QMC_Q4_0, true>(p, ph, sm, full, empty, gk, dead, pos, best);
             else run_matvec<QMC_Q4_0, false>(p, ph, sm, full, empty, gk, dead, pos, best);
         }
-        if (ph.kind == PH_OUT) logits_argmax(p, ph, sm, best);
+        if (ph.kind == PH_OUT) logits_argmax(p, sm, best);
     }
 }
 

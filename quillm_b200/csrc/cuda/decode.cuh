@@ -17,6 +17,7 @@ int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, voi
                         cudaStream_t s);
 
 constexpr int kDecodeHeadsPerUnit = 4;  // query heads per attention work unit
+constexpr int kDecodePartHead = 4;      // floats before acc[] in an attention segment partial
 
 enum DecodePhaseKind : int { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_W2 = 4, PH_OUT = 5 };
 
@@ -29,7 +30,7 @@ struct DecodePhase {
     int rbytes, sbytes;   // split-row bytes per row, scale bytes per row
     int R;                // units per ring stage
     int embed;            // input is the current token's embedding row (first phase)
-    const float *in;      // input vector (x, attention output, SwiGLU output)
+    const float *in;      // input vector (x, SwiGLU output; WO merges the attention partials instead)
     const float *norm_w;  // fused rmsnorm weight or null
     float *out;           // WO/W2: x (+=), FFN: h, OUT: logits
     float *kc, *vc;       // QKV / ATTN: this layer's caches [max_seq][KVl]
@@ -43,7 +44,8 @@ struct DecodeParams {
     const uint8_t *tok;  // embedding table (file layout)
     int dt_tok;
     float *x;  // residual stream
-    float *q, *xb;
+    float *q;
+    float *logits;
     const float2 *rope;
     int *state;  // [token, pos, step, prompt length]
     int vocab;   // valid tokens [0, vocab)
@@ -52,9 +54,8 @@ struct DecodeParams {
     int gen_cap;
     unsigned long long *amax_key;
     int *amax_ctr;
-    unsigned int *gbar;  // grid barrier: [0] arrivals, [1] generation
-    float *apart;        // attention partials [nkv * gsplit][maxseg][4][hd + 2]
-    int *acnt;           // attention merge tickets [nkv * gsplit]
+    unsigned *gbar;  // grid barrier arrival counter (zero between steps)
+    float *apart;    // attention segment partials [nkv * gsplit][maxseg][4][4 + hd]
     int maxseg;
     int *err;
     int nslots, slot_bytes;

@@ -67,7 +67,6 @@ struct qmc_model {
     uint8_t *sout = nullptr;
     unsigned *gbar = nullptr;
     float *apart = nullptr;
-    int *acnt = nullptr;
     int maxseg = 1, gsplit = 1;
 };
 
@@ -297,11 +296,9 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
         const size_t units = (size_t)m->NKVl * m->gsplit;
         RC(dalloc(m, (void **)&m->d_phases, m->phases.size() * sizeof(DecodePhase)));
         RC(dalloc(m, (void **)&m->gbar, 64));
-        RC(dalloc(m, (void **)&m->apart, units * m->maxseg * kDecodeHeadsPerUnit * (m->hd + 2) * 4));
-        RC(dalloc(m, (void **)&m->acnt, units * 4));
+        RC(dalloc(m, (void **)&m->apart, units * m->maxseg * kDecodeHeadsPerUnit * (m->hd + kDecodePartHead) * 4));
         QMC_CUDA(cudaMemcpy(m->d_phases, m->phases.data(), m->phases.size() * sizeof(DecodePhase), cudaMemcpyHostToDevice));
         QMC_CUDA(cudaMemset(m->gbar, 0, 64));
-        QMC_CUDA(cudaMemset(m->acnt, 0, units * 4));
         return QMC_OK;
     }
     if (m->mega && !m->repacked) RC(repack_weights(m));
@@ -318,14 +315,14 @@ int launch_decode_step(qmc_model *m, DevCtx *c) {
     p.scale = 1.0f / sqrtf((float)m->hd);
     p.tok = m->tok;
     p.dt_tok = m->dt_tok;
-    p.x = m->x, p.q = m->q, p.xb = m->xb;
+    p.x = m->x, p.q = m->q, p.logits = m->logits;
     p.rope = m->rope;
     p.state = m->state, p.forced = m->forced, p.gen = m->gen, p.gen_cap = m->S;
     p.vocab = m->V;
     p.amax_key = m->amax;
     p.amax_ctr = (int *)(m->amax + 1);
     p.gbar = m->gbar;
-    p.apart = m->apart, p.acnt = m->acnt, p.maxseg = m->maxseg;
+    p.apart = m->apart, p.maxseg = m->maxseg;
     p.err = c->err;
     p.nslots = m->plan.nslots, p.slot_bytes = m->plan.slot_bytes;
     p.off_bars = m->plan.off_bars, p.off_xq = m->plan.off_xq, p.off_xds = m->plan.off_xds, p.off_red = m->plan.off_red;
@@ -337,7 +334,6 @@ int step_status(qmc_model *m) {
     const int rc = qmc_check_device_error();
     if (rc && m->mega) {
         cudaMemset(m->gbar, 0, 64);
-        cudaMemset(m->acnt, 0, (size_t)m->NKVl * m->gsplit * 4);
         cudaMemset(m->amax, 0, 16);
     }
     return rc;
