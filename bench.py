@@ -223,6 +223,24 @@ def time_prefill(qb, torch, T: int, N: int, K: int, iters: int = 10) -> float:
     return _graph_time(torch, launch, iters)
 
 
+def profile_decode(layers: int) -> None:
+    """--profile-decode LAYERS: a Llama-7B-shaped Q4_0 model with LAYERS layers decodes positions 0..133
+    (a few GB on the device), for ncu captures of decode_step_kernel at a position like the bench's"""
+    import quillm_b200 as qb
+
+    wl = WORKLOADS["llama7b_q4_0"]
+    cfg = dict(wl["cfg"], n_layers=layers)
+    qb.check(qb.cuda().qmc_set_device(0))
+    m = qb.Model(cfg)
+    m.synthesize(wl["dtype"], wl["seed"], STD)
+    m.enqueue_decode(1, 0, 130)
+    qb.check(qb.cuda().qmc_sync())
+    m.enqueue_decode(-1, 0, 4)
+    qb.check(qb.cuda().qmc_sync())
+    print("decode_info", m.decode_info())
+    m.close()
+
+
 def profile_matvec(spec: str) -> None:
     """--profile-matvec ROWSxCOLS:DTYPE[:N]: N plain qmc_matvec launches (for ncu captures)"""
     import torch
@@ -320,8 +338,11 @@ def gpu_arm(args, wl: dict) -> dict | None:
     e2e_s = d.max(time.perf_counter() - t0)
 
     per_gpu_bytes = np.mean([model.step_bytes(p) for p in range(pos0, pos0 + K)])
+    launches, persistent = model.decode_info()
     hbm, tflops, src = peaks()
     step_time = sec / K
+    achieved = per_gpu_bytes / step_time / 1e9
+    kname = "decode_step_kernel (one launch per token)" if persistent else "decode step (per-operation kernels)"
     out = {
         "metric": METRIC, "value": K / sec, "unit": "tok/s", "n_gpus": d.world, "steps": K, "warmup": W,
         "ms_per_step": step_time * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -331,13 +352,16 @@ def gpu_arm(args, wl: dict) -> dict | None:
                    "seq_len": cfg["max_seq"], "prompt_tokens": npos, "decode_positions": [pos0, pos0 + K - 1],
                    "parallelism": f"tp{d.world}",
                    "l2": f"inputs larger than L2: {per_gpu_bytes / 1e9:.2f} GB streamed per step per GPU"},
-        "decode_roofline": {"bound": "hbm", "achieved": per_gpu_bytes / step_time / 1e9, "peak": hbm,
-                            "unit": "GB/s", "frac": per_gpu_bytes / step_time / 1e9 / hbm,
-                            "bytes_per_step_per_gpu": per_gpu_bytes, "peak_source": src},
+        # the dominant kernel: a whole decode step is one launch, so its duration is the step time
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic_from_profiles(f"decode_step {args.workload}")
+                     if persistent and d.world == 1 else None,
+                     "bytes_per_step_per_gpu": per_gpu_bytes,
+                     "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src},
         "prompt_tok_s": npos / prompt_s,
         "e2e": {"value": K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": cfg["vocab_size"] * 4 + 4},
-        "gpu_launches": K * (5 * cfg["n_layers"] + 3),
+        "gpu_launches": K * launches,
         "clocks": clk,
     }
     model.close()
@@ -368,7 +392,7 @@ def kernel_sweeps(qb, torch, wl: dict, hbm: float, tflops: float, src: str) -> d
         tot_t += n * sec
     tag = f"{DTYPE_NAME[wl['dtype']]} decode mix"
     traffic = traffic_from_profiles(f"gemv {DTYPE_NAME[wl['dtype']]} 11008x4096")
-    res["roofline"] = {"bound": "hbm", "kernel": f"gemv_q_kernel<{DTYPE_NAME[wl['dtype']].upper()}> ({tag})",
+    res["matvec_roofline"] = {"bound": "hbm", "kernel": f"gemv_q_kernel<{DTYPE_NAME[wl['dtype']].upper()}> ({tag})",
                        "achieved": tot_b / tot_t / 1e9, "peak": hbm, "unit": "GB/s",
                        "frac": tot_b / tot_t / 1e9 / hbm, "traffic": traffic,
                        "traffic_note": "DRAM bytes per 11008x4096 launch from ncu (algorithmic 25.43 MB)",
@@ -496,9 +520,14 @@ def main():
     ap.add_argument("--prompt", type=int, default=None, help="override the workload's prompt length")
     ap.add_argument("--profile-matvec", default=None, metavar="ROWSxCOLS:DTYPE[:N]",
                     help="only launch N plain matvecs (a small case for ncu captures)")
+    ap.add_argument("--profile-decode", type=int, default=None, metavar="LAYERS",
+                    help="only decode 134 positions of a Llama-7B-shaped Q4_0 model with LAYERS layers (ncu)")
     args = ap.parse_args()
     if args.profile_matvec:
         profile_matvec(args.profile_matvec)
+        return
+    if args.profile_decode:
+        profile_decode(args.profile_decode)
         return
     if args.warmup < 3:
         args.warmup = 3

@@ -144,6 +144,10 @@ int qmc_model_logits(qmc_model *m, const float **dev_logits);
 int qmc_model_config(const qmc_model *m, qmc_config *cfg);
 /* device bytes read per decode step at position pos (weights + KV), for roofline accounting */
 int qmc_model_step_bytes(const qmc_model *m, int32_t pos, double *bytes);
+/* how a decode step runs, fixed by the first step: *launches = kernel launches per step (1 for the
+ * single-launch persistent path: one GPU, Q8_0/Q4_0 matrices; otherwise one per operation), *persistent =
+ * 1 for that path.  Before the first step both are 0. */
+int qmc_model_decode_info(const qmc_model *m, int32_t *launches, int32_t *persistent);
 int qmc_model_free(qmc_model *m);
 
 #pragma GCC visibility pop

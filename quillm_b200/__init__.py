@@ -99,6 +99,7 @@ _CUDA_SIGS = {
     "qmc_model_logits": (I, [V, C.POINTER(V)]),
     "qmc_model_config": (I, [V, C.POINTER(QmcConfig)]),
     "qmc_model_step_bytes": (I, [V, I32, C.POINTER(D)]),
+    "qmc_model_decode_info": (I, [V, C.POINTER(I32), C.POINTER(I32)]),
     "qmc_model_free": (I, [V]),
 }
 
@@ -235,6 +236,12 @@ class Model:
         b = C.c_double(0)
         check(self.lib.qmc_model_step_bytes(self.h, pos, C.byref(b)), "step_bytes")
         return b.value
+
+    def decode_info(self) -> tuple[int, bool]:
+        """(kernel launches per decode step, whether the single-launch persistent path runs)"""
+        n, pers = C.c_int32(0), C.c_int32(0)
+        check(self.lib.qmc_model_decode_info(self.h, C.byref(n), C.byref(pers)), "decode_info")
+        return n.value, bool(pers.value)
 
     def close(self) -> None:
         if self.h:

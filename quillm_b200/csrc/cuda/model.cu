@@ -686,6 +686,18 @@ int qmc_model_step_bytes(const qmc_model *m, int32_t pos, double *bytes) {
     return QMC_OK;
 }
 
+int qmc_model_decode_info(const qmc_model *m, int32_t *launches, int32_t *persistent) {
+    if (!m || !launches || !persistent) return set_error(QMC_EINVAL, "decode_info: null argument");
+    *persistent = m->mega ? 1 : 0;
+    if (!m->graph) *launches = 0;
+    else if (m->mega) *launches = 1;
+    else {  // embed + per layer {qkv, attention, wo, w1/w3, w2} + output (+ argmax when not fused)
+        const bool fused = m->tp == 1 && m->dt_out != QMC_F32;
+        *launches = 2 + 5 * m->L + (fused ? 0 : 1);
+    }
+    return QMC_OK;
+}
+
 int qmc_model_free(qmc_model *m) {
     if (!m) return QMC_OK;
     cudaSetDevice(m->dev);
