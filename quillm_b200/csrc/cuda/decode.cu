@@ -554,7 +554,9 @@ __device__ __forceinline__ void unit_dot(const uint8_t *r0, int rbytes, int sbyt
 
 // One matvec phase on this CTA's units.  Group grp takes the stages g with g % NG == grp; within the
 // group the units of its stages are dealt round-robin to its 4 warps, so a warp works alone: its own
-// row dots, its own warp sum, its own epilogue (lane 0), and one arrival on each of its group's stages.
+// row dots and warp sums, and one arrival on each of its group's stages.  Epilogues are deferred: lane
+// k keeps the k-th pending unit's sums, and every 32 units (and at the end of the phase) all lanes run
+// their epilogues at once, their operand loads (RoPE pairs, residual x) in flight together.
 template <int DT, bool TWO>
 __device__ void run_matvec(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, uint64_t *full, uint64_t *empty,
                            unsigned &gk, bool &dead, int pos, unsigned long long &best) {
@@ -581,6 +583,16 @@ __device__ void run_matvec(const DecodeParams &p, const DecodePhase &ph, uint8_t
     split_units(ph.units, u0, u1);
     const int nst = (int)((u1 - u0 + R - 1) / R);
     int uoff = 0;  // units in this group's earlier stages of the phase
+    float pa0 = 0.0f, pa1 = 0.0f;  // this lane's pending unit: sums and index
+    int64_t punit = 0;
+    int npend = 0;  // pending units in the warp (warp-uniform)
+    auto flush = [&]() {
+        if (lane < npend) {
+            const float2 opnd = epilogue_operand(p, ph, punit, pos);
+            epilogue(p, ph, punit, pa0, pa1, opnd, pos, best);
+        }
+        npend = 0;
+    };
     for (int k = 0; k < nst; k++) {
         const unsigned g = gk + (unsigned)k;
         if ((int)(g % NG) != grp) continue;
@@ -594,17 +606,17 @@ __device__ void run_matvec(const DecodeParams &p, const DecodePhase &ph, uint8_t
         const uint8_t *stage = sm + (size_t)s * p.slot_bytes;
         if (!dead) {
             for (int i = (wig - uoff % GW + GW) % GW; i < n; i += GW) {
-                // the epilogue operand is fetched first so its latency hides behind the dots
-                const float2 opnd = lane == 0 ? epilogue_operand(p, ph, ua + i, pos) : make_float2(0.0f, 0.0f);
                 float a0, a1;
                 unit_dot<DT, TWO>(stage + (int64_t)i * UR * rbytes, rbytes, sbytes, nb, xq, xds, xw, xd, xs, a0, a1);
-                if (lane == 0) epilogue(p, ph, ua + i, a0, a1, opnd, pos, best);
+                if (lane == npend) pa0 = a0, pa1 = a1, punit = ua + i;
+                if (++npend == 32) flush();
             }
         }
         uoff += n;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    if (!dead) flush();
     gk += (unsigned)nst;
 }
 
