@@ -7,17 +7,19 @@
 // takes ~3 us to land under load, so an SM needs ~130 KB in flight to draw its share of the bandwidth.
 // Separate kernels per matvec cannot keep that: each boundary drains the pipeline, and co-residency
 // with the next kernel caps the ring at half the shared memory.  Here one producer warp per CTA walks
-// the weight stages of ALL phases in order through a ring of 15 (or 12, 9, 6, 3) slots in ~210 KB of shared
+// the weight stages of ALL phases in order through a ring of 22 (or 11) slots in ~215 KB of shared
 // memory and never waits on a grid barrier: while the consumers sit in a barrier, an activation
 // prologue or the attention phase, the producer is already streaming the next matrices.
 //
-// Consumers: 12 warps in 3 groups; global stage g goes to group g % 3 and slot g % nslots (nslots is a
-// multiple of 3, so a slot always serves one group and the parity waits stay one phase apart).  The
-// units (rows, or the RoPE / SwiGLU row pairs) of a group's stages are dealt round-robin to its 4 warps
-// and a warp works alone: lane l takes blocks l, l+32, ... of the row (the first four held in registers
-// as Q8_0 activations for the whole phase), a warp sum forms the row dot and lane 0 runs the epilogue
-// (RoPE + K/V store, residual add, SwiGLU, logits + argmax key).  No CTA or group barrier runs inside
-// the stream loop.
+// Consumers: 11 warps, each its own stage group; global stage g goes to warp g % 11 and slot g % nslots
+// (nslots is a multiple of 11, so a slot always serves one warp and the parity waits stay one phase
+// apart).  A warp works alone on the units (rows, or the RoPE / SwiGLU row pairs) of its stages: lane l
+// takes blocks l, l+32, ... of the row (the first four held in registers as Q8_0 activations for the
+// whole phase), a warp sum forms the row dot and the epilogues (RoPE + K/V store, residual add, SwiGLU,
+// logits + argmax key) run 32 units at a time across the lanes.  No CTA barrier runs inside the stream
+// loop.  12 warps in all leave each thread 168 registers (at most 3 warps per SM sub-partition); with 13
+// the cap is 128 and the kernel spills to local memory, whose reloads miss the small L1 left beside the
+// ring and cost an L2 round trip each.
 //
 // Weights are in the split-row layout (decode.cuh): aligned 16-byte shared loads per block, no realignment.
 // Per block the arithmetic is the reference's (src/kernels_scalar.c:12-34): integer block dot (dp4a; Q4_0
@@ -25,7 +27,7 @@
 // s += (float)acc * (dW * dX).  Activations are quantized per phase by every CTA (bit-exact Q8_0,
 // src/quant.c:33-53) after the fused rmsnorm (src/ops.c:93-98).
 //
-// Attention (src/model.c:132-156): (KV head, position segment) units over the CTAs; the 12 warps of a
+// Attention (src/model.c:132-156): (KV head, position segment) units over the CTAs; the 11 warps of a
 // CTA walk the segment's positions with an online softmax per query head and merge in shared memory;
 // each segment's (max, sum, acc) partial goes to global memory and the wo phase's prologue merges the
 // segments of a head while it quantizes the attention output (no extra barrier or ticket).
@@ -39,10 +41,10 @@
 namespace qmc {
 namespace {
 
-constexpr int NCW = 12;             // consumer warps (13 warps in all: at most 4 per SM sub-partition, so
-                                    // each thread may hold 128 registers)
-constexpr int NG = 3, GW = 4;       // groups x warps per group
-constexpr int GT = GW * 32;         // threads per group
+constexpr int NCW = 11;             // consumer warps (12 warps in all: at most 3 per SM sub-partition, so
+                                    // each thread may hold 168 registers; with 13 warps the cap is 128 and
+                                    // the whole-step kernel spills)
+constexpr int NG = NCW, GW = 1;     // stage groups x warps per group: each warp consumes its own stages
 constexpr int NT = (NCW + 1) * 32;  // + the producer warp
 constexpr int NCT = NCW * 32;       // consumer threads
 constexpr int QPR = NCT / 2;        // activation blocks per prologue round (2 threads per block)
@@ -53,13 +55,72 @@ constexpr int kMinAttnPos = 32;     // an attention segment spans at least this 
 constexpr int kAttnChunk = 4;       // positions per warp whose K/V rows are loaded together
 constexpr int kPartHead = kDecodePartHead;  // partial: (max, sum, 2 pad, acc[hd]), acc 16-byte aligned
 constexpr int kFastSegs = 4;        // segment partials the wo prologue merges with all loads in flight
-// named barriers: 0 = __syncthreads, 1..NG = the groups, kBarConsumers = all consumer warps
-constexpr int kBarConsumers = NG + 1;
+// named barriers: 0 = __syncthreads, kBarConsumers = all consumer warps (the producer warp never waits)
+constexpr int kBarConsumers = 1;
 // shared scratch at off_red: prologue partial sums, argmax keys, grid-barrier flag
 constexpr int kRedDred = 0, kRedKeys = 128;
-constexpr int kRedFlag = kRedKeys + NCW * 8, kRedDesc = kRedFlag + 128;
+constexpr int kRedFlag = kRedKeys + (NCW * 8 + 15) / 16 * 16, kRedDesc = kRedFlag + 128;
 constexpr int kRedBytes = kRedDesc + 2 * (int)sizeof(DecodePhase);  // + this and the next phase's descriptor
 static_assert(sizeof(DecodePhase) % 16 == 0, "descriptors are copied in 16-byte chunks");
+static_assert(kRedDesc % 16 == 0 && NCW * 8 <= kRedKeys, "shared scratch layout");
+static_assert(NG <= 31, "one producer lane per stage group");
+
+// ---------------------------------------------------------------- optional timing stamps
+// Compiled in only with -DQMC_DECODE_TRACE (a profiling build of the library; the default build has no
+// trace code): per phase and CTA, kTrSlots 64-bit words of globaltimer stamps (ns) and counters, written
+// to the buffer given to qmc_decode_trace_set.
+#ifdef QMC_DECODE_TRACE
+__constant__ unsigned long long *g_dtrace;  // constant bank: read without a global round trip
+#endif
+enum : int {
+    kTrStart = 0,  // consumers pass the phase's grid barrier (thread 0)
+    kTrProEnd,     // activation prologue (or attention) done
+    kTrMvEnd,      // last warp leaves the matvec (max over warps)
+    kTrArrive,     // CTA arrives at the barrier that ends the phase
+    kTrProdFirst,  // producer issues the phase's first stage
+    kTrProdLast,   // ... and its last
+    kTrProdWait,   // producer time waiting for free slots in the phase (SM cycles)
+    kTrFullWait,   // consumer warps' time waiting for full stages (cycles, summed over warps)
+    kTrUnits,      // units the CTA's warps computed
+    kTrFlush,      // consumer warps' time in epilogue flushes (cycles, summed)
+    kTrDot,        // consumer warps' time in row dots (cycles, summed)
+    kTrSlots = 16
+};
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// a stamp taken only once x is computed (x is an input of the asm)
+__device__ __forceinline__ unsigned long long gtime_after(float x) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t) : "f"(x));
+    return t;
+}
+__device__ __forceinline__ unsigned long long *trace_slot(int ph, int k) {
+#ifdef QMC_DECODE_TRACE
+    return g_dtrace ? g_dtrace + ((size_t)ph * gridDim.x + blockIdx.x) * kTrSlots + k : nullptr;
+#else
+    (void)ph, (void)k;
+    return nullptr;
+#endif
+}
+// CTA 0 also records every stage g < kTrStages: [g][0] issued, [1] consumer saw it full, [2] released
+constexpr int kTrStages = 4096;
+__device__ __forceinline__ unsigned long long *trace_stage(const DecodeParams &p, unsigned g, int k) {
+#ifdef QMC_DECODE_TRACE
+    return (g_dtrace && blockIdx.x == 0 && g < (unsigned)kTrStages)
+               ? g_dtrace + (size_t)p.nph * gridDim.x * kTrSlots + (size_t)g * 4 + k
+               : nullptr;
+#else
+    (void)p, (void)g, (void)k;
+    return nullptr;
+#endif
+}
+// the value expression is evaluated only in a trace build with a buffer set
+#define DTRACE_SET(ph, k, v) do { if (unsigned long long *q_ = trace_slot(ph, k)) *q_ = (v); } while (0)
+#define DTRACE_ADD(ph, k, v) do { if (unsigned long long *q_ = trace_slot(ph, k)) atomicAdd(q_, (unsigned long long)(v)); } while (0)
+#define DTRACE_MAX(ph, k, v) do { if (unsigned long long *q_ = trace_slot(ph, k)) atomicMax(q_, (unsigned long long)(v)); } while (0)
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -95,6 +156,7 @@ __device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, b
     named_sync(kBarConsumers, NCT);
     if (threadIdx.x == 0) {
         int ok = 1;
+        DTRACE_SET((int)(target / gridDim.x) - 1, kTrArrive, gtime());
         red_release_add(p.gbar, 1u);
         if (!dead) {
             const long long t0 = clock64();
@@ -125,23 +187,62 @@ __device__ __forceinline__ void desc_prefetch(const DecodePhase *src, DecodePhas
 __device__ __forceinline__ void desc_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // ---------------------------------------------------------------- producer
+// The producer warp walks this CTA's weight range of every matvec phase in stages of R units.  Global
+// stage g belongs to consumer warp g % NG and goes to slot g % nslots; lane w < NG of the producer warp
+// serves consumer warp w alone: it copies that warp's stages in order, each into its slot as soon as the
+// warp released the slot's previous stage, so a slow warp never holds up another warp's refills.  The
+// producer never waits on a grid barrier: while the consumers sit in a barrier, an activation prologue
+// or attention, every warp's slots fill with its next stages, of the next phases too.
 __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uint64_t *empty) {
-    unsigned gk = 0;
-    for (int i = 0; i < p.nph; i++) {
-        const DecodePhase &ph = p.ph[i];
-        if (ph.kind == PH_ATTN) continue;
-        int64_t u0, u1;
-        split_units(ph.units, u0, u1);
-        const int64_t ubytes = (int64_t)ph.urows * ph.rbytes;
-        for (int64_t ua = u0; ua < u1; ua += ph.R, gk++) {
-            const int s = (int)(gk % (unsigned)p.nslots);
-            if (gk >= (unsigned)p.nslots && !mbar_wait(&empty[s], ((gk / p.nslots) - 1) & 1u)) {
-                raise_error(p.err, kErrMbarTimeout);
+    const int w = threadIdx.x & 31;
+    if (w >= NG) return;
+    // cursor: phase i (a matvec phase or p.nph when done), stage k within it, G = global index of its
+    // stage 0, this CTA's units [u0, u1) of it
+    int i = -1, k = w;
+    unsigned G = 0;
+    int64_t u0 = 0, u1 = 0, ubytes = 0;
+    int nst = 0;
+    auto settle = [&]() {  // move the cursor onto the phase that holds stage G + k
+        while (i < p.nph && (i < 0 || k >= nst)) {
+            if (i >= 0) k -= nst, G += (unsigned)nst;
+            while (++i < p.nph && p.ph[i].kind == PH_ATTN) {
+            }
+            if (i >= p.nph) break;
+            const DecodePhase &q = p.ph[i];
+            split_units(q.units, u0, u1);
+            ubytes = (int64_t)q.urows * q.rbytes;
+            nst = (int)((u1 - u0 + q.R - 1) / q.R);
+        }
+    };
+    settle();
+    const long long t0 = clock64();
+    while (true) {
+        bool done = i >= p.nph, issued = false;
+        if (!done) {
+            const unsigned g = G + (unsigned)k;
+            const int s = (int)(g % (unsigned)p.nslots);
+            if (g < (unsigned)p.nslots || mbar_test(&empty[s], ((g / p.nslots) - 1) & 1u)) {
+                const DecodePhase &q = p.ph[i];
+                const int64_t ua = u0 + (int64_t)k * q.R;
+                const uint32_t bytes = (uint32_t)(min((int64_t)q.R, u1 - ua) * ubytes);
+                if (k == 0) DTRACE_SET(i, kTrProdFirst, gtime());
+                if (k + NG >= nst) DTRACE_MAX(i, kTrProdLast, gtime());
+                if (unsigned long long *q_ = trace_stage(p, g, 0)) *q_ = gtime();
+                mbar_arrive_tx(&full[s], bytes);
+                bulk_g2s(sm + (size_t)s * p.slot_bytes, q.W + ua * ubytes, bytes, &full[s]);
+                k += NG;
+                settle();
+                issued = true;
+            }
+        }
+        constexpr unsigned kLanes = (1u << NG) - 1u;  // lanes 0..NG-1 run this loop together
+        if (!__any_sync(kLanes, !done)) return;
+        if (!__any_sync(kLanes, issued)) {  // every lane waits on a slot: back off briefly
+            __nanosleep(64);
+            if (__any_sync(kLanes, clock64() - t0 > kWaitCycles)) {  // warp-uniform: all lanes leave together
+                if (!done) raise_error(p.err, kErrMbarTimeout);
                 return;
             }
-            const uint32_t bytes = (uint32_t)(min((int64_t)ph.R, u1 - ua) * ubytes);
-            mbar_arrive_tx(&full[s], bytes);
-            bulk_g2s(sm + (size_t)s * p.slot_bytes, ph.W + ua * ubytes, bytes, &full[s]);
         }
     }
 }
@@ -199,7 +300,8 @@ __device__ void attn_out16(const DecodeParams &p, int64_t e0, int K, int nseg, f
         for (int i = 0; i < 16; i++) v[i] = num[i] * rden;
         return;
     }
-    for (int i = 0; i < 16; i++) {  // generic: element by element
+#pragma unroll
+    for (int i = 0; i < 16; i++) {  // generic: element by element (zero past K)
         const int64_t e = e0 + i;
         if (e >= K) {
             v[i] = 0.0f;
@@ -222,66 +324,55 @@ __device__ void attn_out16(const DecodeParams &p, int64_t e0, int K, int nseg, f
     }
 }
 
-// 16 elements e0..e0+15 of the phase input: the token's embedding row (dequantized as src/quant.c:65-94,
-// one rounding) for the first phase, the merged attention output for wo, else the input vector; zero
-// past K
-__device__ __forceinline__ void fetch16(const DecodeParams &p, const DecodePhase &ph, const uint8_t *erow, int64_t e0,
-                                        int nseg, float (&v)[16]) {
-    const int K = ph.K;
+// 16 elements e0..e0+15 of the token's embedding row (dequantized as src/quant.c:65-94, one rounding);
+// zero past K
+__device__ __forceinline__ void embed16(const DecodeParams &p, const uint8_t *erow, int64_t e0, int K,
+                                        float (&v)[16]) {
     if (e0 >= K) {  // pairs past the last block (their block and its scale lie outside the row)
 #pragma unroll
         for (int i = 0; i < 16; i++) v[i] = 0.0f;
         return;
     }
-    if (ph.embed) {
-        const int64_t b = e0 >> 5;
-        const int j0 = (int)(e0 & 31);
-        if (p.dt_tok == QMC_F32) {
+    const int64_t b = e0 >> 5;
+    const int j0 = (int)(e0 & 31);
+    if (p.dt_tok == QMC_F32) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? ((const float *)erow)[e0 + i] : 0.0f;
-        } else if (p.dt_tok == QMC_Q8_0) {
-            const uint8_t *blk = erow + b * kQ8Bytes;
-            const float d = h2f(blk[0] | (blk[1] << 8));
+        for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? ((const float *)erow)[e0 + i] : 0.0f;
+    } else if (p.dt_tok == QMC_Q8_0) {
+        const uint8_t *blk = erow + b * kQ8Bytes;
+        const float d = h2f(blk[0] | (blk[1] << 8));
 #pragma unroll
-            for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? d * (float)(int8_t)blk[2 + j0 + i] : 0.0f;
-        } else {
-            const uint8_t *blk = erow + b * kQ4Bytes;
-            const float d = h2f(blk[0] | (blk[1] << 8));
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const int k = j0 + i, byte = blk[2 + (k >> 1)];
-                v[i] = e0 + i < K ? d * (float)(((k & 1) ? (byte >> 4) : (byte & 15)) - 8) : 0.0f;
-            }
-        }
-        return;
-    }
-    if (ph.kind == PH_WO) {
-        attn_out16(p, e0, K, nseg, v);
-        return;
-    }
-    const float *src = ph.in + e0;
-    if (e0 + 16 <= K && !((uintptr_t)src & 15)) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 a = __ldcg((const float4 *)src + i);
-            v[4 * i] = a.x, v[4 * i + 1] = a.y, v[4 * i + 2] = a.z, v[4 * i + 3] = a.w;
-        }
+        for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? d * (float)(int8_t)blk[2 + j0 + i] : 0.0f;
     } else {
+        const uint8_t *blk = erow + b * kQ4Bytes;
+        const float d = h2f(blk[0] | (blk[1] << 8));
 #pragma unroll
-        for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? __ldcg(src + i) : 0.0f;
+        for (int i = 0; i < 16; i++) {
+            const int k = j0 + i, byte = blk[2 + (k >> 1)];
+            v[i] = e0 + i < K ? d * (float)(((k & 1) ? (byte >> 4) : (byte & 15)) - 8) : 0.0f;
+        }
     }
 }
-__device__ __forceinline__ void fetch16_w(const float *w, int64_t e0, int K, float (&v)[16]) {
-    if (e0 + 16 <= K && !((uintptr_t)(w + e0) & 15)) {
+
+// 16 elements e0..e0+15 of a float vector, zero past K; CG: through L2 only (vectors other CTAs wrote
+// during this step), else the default path (weights that stay fixed).  w is 16-byte aligned and its
+// allocation extends past element K by at least 15 floats (every model buffer is its own cudaMalloc with
+// 256 bytes of slack), e0 is a multiple of 16: four vector loads, then the tail past K masked to zero.
+template <bool CG>
+__device__ __forceinline__ void load16(const float *w, int64_t e0, int K, float (&v)[16]) {
+    if (e0 >= K) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float4 a = *((const float4 *)(w + e0) + i);
-            v[4 * i] = a.x, v[4 * i + 1] = a.y, v[4 * i + 2] = a.z, v[4 * i + 3] = a.w;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? w[e0 + i] : 0.0f;
+        for (int i = 0; i < 16; i++) v[i] = 0.0f;
+        return;
     }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float4 *q = (const float4 *)(w + e0) + i;
+        const float4 a = CG ? __ldcg(q) : *q;
+        v[4 * i] = a.x, v[4 * i + 1] = a.y, v[4 * i + 2] = a.z, v[4 * i + 3] = a.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = e0 + i < K ? v[i] : 0.0f;
 }
 
 // activation block b is stored with its 16-byte halves swapped when bit 2 of b is set, so 8 threads
@@ -294,24 +385,21 @@ __device__ __forceinline__ int xswz(int b) { return ((b >> 2) & 1) << 4; }
 constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
 constexpr int kRoundBits = 0x4B400000;
 
-// Quotients v / sc for the quantizer (src/quant.c:47-50 divides, then rounds half to even).  |v / sc| <
-// 256, so r = v * (1 / sc) lies within 4.6e-5 of the correctly rounded quotient and rounds to the same
-// integer unless that quotient is within 4.6e-5 of a half-integer.  If any of the lane's 16 products is
-// that close, the lane takes the IEEE divisions instead (rare); NaN and infinity give the same results
-// on both paths.
-__device__ __forceinline__ void quotients16(const float (&v)[16], float sc, float (&r)[16]) {
-    const float rs = __frcp_rn(sc);
-    bool near = false;
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-        r[i] = __fmul_rn(v[i], rs);
-        const float n = __fsub_rn(__fadd_rn(r[i], kRound), kRound);  // nearest integer
-        near |= fabsf(__fsub_rn(r[i], n)) > 0.4999f;
-    }
-    if (near) {
-#pragma unroll
-        for (int i = 0; i < 16; i++) r[i] = __fdiv_rn(v[i], sc);
-    }
+// rint(RN(v / sc)) for an element whose product r = v * (1 / sc) lies within 1e-4 of a half-integer,
+// without dividing (rare).  h = floor(r) + 0.5 is that half-integer; h * sc has at most 20 significant
+// bits, so it and d = v - h * sc (Sterbenz: v and h * sc are within 0.1% of each other) are exact.
+// RN(v / sc) equals h exactly when v / sc lies inside h's rounding interval, [h - u, h + u] with
+// u = ulp(h) / 2 (the side towards zero is u / 2 when |h| = 0.5, a power of two), ties included since
+// h's last mantissa bit is 0; rint then takes the even neighbour, else the side d points to.
+__device__ __forceinline__ int quant_near_half(float v, float r, float sc) {
+    const float fl = floorf(r), h = fl + 0.5f;
+    const float d = fmaf(-h, sc, v);
+    const float u = __int_as_float((__float_as_int(h) & 0x7f800000) - (24 << 23));  // ulp(h) / 2, |h| >= 0.5
+    const bool toward0 = (d < 0.0f) == (h > 0.0f);
+    const float lim = __fmul_rn((fabsf(h) == 0.5f && toward0) ? 0.5f * u : u, sc);
+    const int f = __float_as_int(__fadd_rn(fl, kRound)) - kRoundBits;  // floor(r) as an integer
+    const int q = fabsf(d) <= lim ? f + (f & 1) : (d > 0.0f ? f + 1 : f);
+    return min(127, max(-127, q));
 }
 
 // Q8_0 of block b held by a lane pair (part j: elements 16j..16j+15), bit-exact with src/quant.c:33-53:
@@ -332,95 +420,113 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
         for (int i = 0; i < w; i++) m[i] = max(m[i], m[i + w]);
     const uint32_t ab = max(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
     const float sc = h2f(f2h(__fdiv_rn(__uint_as_float(ab), 127.0f)));
-    float qf[16];
-    quotients16(v, sc, qf);
-    int q[16];
+    const float rs = __frcp_rn(sc);
+    // q = rint(v / sc) clamped to +-127, as v * (1 / sc) + 1.5 * 2^23 (round to nearest even, no
+    // float->int conversion).  |v / sc| < 256, so v * (1 / sc) lies within 4.6e-5 of the correctly
+    // rounded quotient and rounds to the same integer unless it is within 1e-4 of a half-integer; those
+    // elements take quant_near_half.  NaN gives 0.
+    uint32_t w[4] = {0u, 0u, 0u, 0u};  // the 16 quants in element order, 4 per word
+    int sum = 0;
+    bool near = false;
 #pragma unroll
     for (int i = 0; i < 16; i++) {
-        const float c = fminf(fmaxf(qf[i], -127.0f), 127.0f);
-        q[i] = (sc != 0.0f && qf[i] == qf[i]) ? __float_as_int(__fadd_rn(c, kRound)) - kRoundBits : 0;
+        const float r = __fmul_rn(v[i], rs);
+        const float c = fminf(fmaxf(r, -127.0f), 127.0f);
+        const float cr = __fadd_rn(c, kRound);
+        const int q = (sc != 0.0f && r == r) ? __float_as_int(cr) - kRoundBits : 0;
+        near |= fabsf(__fsub_rn(r, __fsub_rn(cr, kRound))) > 0.4999f;
+        sum += q;
+        w[i >> 2] |= (uint32_t)(q & 0xff) << (8 * (i & 3));
     }
-    int sum = 0;
+    if (near) {  // rare: redo the lane's elements, the near-half ones exactly
+        sum = 0;
 #pragma unroll
-    for (int i = 0; i < 16; i += 4) sum += (q[i] + q[i + 1]) + (q[i + 2] + q[i + 3]);
+        for (int i = 0; i < 16; i++) {
+            const float r = __fmul_rn(v[i], rs);
+            const float c = fminf(fmaxf(r, -127.0f), 127.0f);
+            const float cr = __fadd_rn(c, kRound);
+            int q = (sc != 0.0f && r == r) ? __float_as_int(cr) - kRoundBits : 0;
+            if (fabsf(__fsub_rn(r, __fsub_rn(cr, kRound))) > 0.4999f) q = quant_near_half(v[i], r, sc);
+            sum += q;
+            const uint32_t m = 0xffu << (8 * (i & 3));
+            w[i >> 2] = (w[i >> 2] & ~m) | ((uint32_t)(q & 0xff) << (8 * (i & 3)));
+        }
+    }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     if (!active) return;
-    auto pk = [&](int a, int b2, int c, int d) {
-        return (uint32_t)(q[a] & 0xff) | ((uint32_t)(q[b2] & 0xff) << 8) | ((uint32_t)(q[c] & 0xff) << 16) |
-               ((uint32_t)q[d] << 24);
-    };
     uint8_t *blk = xq + (int64_t)b * 32;
     const int sw = xswz(b);
     if (!q4) {
-        *(uint4 *)(blk + ((16 * j) ^ sw)) = make_uint4(pk(0, 1, 2, 3), pk(4, 5, 6, 7), pk(8, 9, 10, 11), pk(12, 13, 14, 15));
-    } else {
-        *(uint2 *)(blk + ((8 * j) ^ sw)) = make_uint2(pk(0, 2, 4, 6), pk(8, 10, 12, 14));
-        *(uint2 *)(blk + ((16 + 8 * j) ^ sw)) = make_uint2(pk(1, 3, 5, 7), pk(9, 11, 13, 15));
+        *(uint4 *)(blk + ((16 * j) ^ sw)) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {  // even elements (bytes 0, 2 of each word pair), then odd ones
+        *(uint2 *)(blk + ((8 * j) ^ sw)) = make_uint2(__byte_perm(w[0], w[1], 0x6420), __byte_perm(w[2], w[3], 0x6420));
+        *(uint2 *)(blk + ((16 + 8 * j) ^ sw)) = make_uint2(__byte_perm(w[0], w[1], 0x7531), __byte_perm(w[2], w[3], 0x7531));
     }
     if (j == 0) xds[b] = make_int2(__float_as_int(sc), sum);
 }
 
-// The phase input (optionally x * inv * w, inv = (float)(1 / sqrt(sum_double(x^2)/n + eps)),
-// src/ops.c:93-98) quantized into shared memory by the consumer threads, two per block; the first
-// phase's CTA 0 also stores the embedding into x.  The first round's x and w stay in registers.
+// The phase input quantized into shared memory by the consumer threads, two per block: one loop over the
+// rounds of QPR blocks, with one load site and one quantization site for every kind of phase, so the
+// instruction footprint the SMs cycle through each layer stays small:
+//  - rmsnorm phases (QKV, FFN, OUT): x * inv * w, inv = (float)(1 / sqrt(sum_double(x^2)/n + eps))
+//    (src/ops.c:93-98), x the residual stream or, in the step's first phase, the token's embedding
+//    (which CTA 0 also stores into x).  With one round, x and w are loaded together and x stays in
+//    registers across the block sum; longer rows take a first pass for the sum;
+//  - WO: the attention output, merged from the segment partials;
+//  - W2: the SwiGLU output.
+// Threads past the row's blocks load zeros and store nothing.
 __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int token, int pos) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, qd = t >> 1, j = t & 1;
     uint8_t *xq = sm + p.off_xq;
     int2 *xds = (int2 *)(sm + p.off_xds);
-    const bool q4 = ph.dtype == QMC_Q4_0;
+    const bool q4 = ph.dtype == QMC_Q4_0, norm = ph.norm_w != nullptr;
     const int K = ph.K, rounds = (ph.nb + QPR - 1) / QPR;
+    const bool two_pass = norm && rounds > 1;  // a sum pass over all rounds, then the quantizing pass
     const uint8_t *erow = ph.embed ? p.tok + (int64_t)token * row_bytes(p.dt_tok, K) : nullptr;
     const bool keep_x = ph.embed && blockIdx.x == 0;
-    const float *nw = ph.norm_w;
-    const int nseg = attn_segments(p, pos);
-    const int64_t e00 = (int64_t)qd * 32 + 16 * j;
-    float v0[16], w0[16];
-    fetch16(p, ph, erow, e00, nseg, v0);
-    if (nw) fetch16_w(nw, e00, K, w0);
+    const int nseg = ph.kind == PH_WO ? attn_segments(p, pos) : 0;
+    double ss = 0.0;
     float inv = 1.0f;
-    if (nw) {
-        double ss = 0.0;
-#pragma unroll
-        for (int i = 0; i < 16; i++) ss = fma((double)v0[i], (double)v0[i], ss);
-        for (int r = 1; r < rounds; r++) {
-            float v[16];
-            fetch16(p, ph, erow, (int64_t)(r * QPR + qd) * 32 + 16 * j, nseg, v);
-#pragma unroll
-            for (int i = 0; i < 16; i++) ss = fma((double)v[i], (double)v[i], ss);
-        }
-        ss = warp_sum_d(ss);
-        double *dred = (double *)(sm + p.off_red + kRedDred);
-        if (lane == 0) dred[warp] = ss;
-        named_sync(kBarConsumers, NCT);
-        double tot = 0.0;
-#pragma unroll
-        for (int w = 0; w < NCW; w++) tot += dred[w];  // same order in every thread
-        inv = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
-    }
-    float v1[16], w1[16];
-    for (int r = 0; r < rounds; r++) {
-        if (r * QPR + warp * 16 >= ph.nb) break;  // this warp's blocks (and later rounds') are past the row
+#pragma unroll 1
+    for (int it = 0; it < (two_pass ? 2 * rounds : rounds); it++) {
+        const bool sum_pass = two_pass && it < rounds;
+        const int r = two_pass && !sum_pass ? it - rounds : it;
         const int b = r * QPR + qd;
         const int64_t e0 = (int64_t)b * 32 + 16 * j;
-        if (r > 0) {
+        float v[16], w[16];
+        if (erow) embed16(p, erow, e0, K, v);
+        else if (ph.kind == PH_WO) attn_out16(p, e0, K, nseg, v);
+        else load16<true>(ph.in, e0, K, v);
+        if (norm && !sum_pass) load16<false>(ph.norm_w, e0, K, w);  // in flight with v
+        if (norm && (sum_pass || !two_pass)) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) v0[i] = v1[i], w0[i] = w1[i];
+            for (int i = 0; i < 16; i++) ss = fma((double)v[i], (double)v[i], ss);
+            if (it == rounds - 1) {  // the block's sum, same order in every warp
+                ss = warp_sum_d(ss);
+                double *dred = (double *)(sm + p.off_red + kRedDred);
+                if (lane == 0) dred[warp] = ss;
+                named_sync(kBarConsumers, NCT);
+                float invl = 0.0f;
+                if (lane == 0) {  // one lane per warp: double division and sqrt are slow
+                    double tot = 0.0;
+#pragma unroll
+                    for (int k = 0; k < NCW; k++) tot += dred[k];
+                    invl = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
+                }
+                inv = __shfl_sync(0xffffffffu, invl, 0);
+            }
         }
-        if (r + 1 < rounds) {  // next round's loads in flight while this one is quantized
-            const int64_t e1 = e0 + (int64_t)QPR * 32;
-            fetch16(p, ph, erow, e1, nseg, v1);
-            if (nw) fetch16_w(nw, e1, K, w1);
-        }
+        if (sum_pass) continue;
         if (keep_x) {
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                if (e0 + i < K) __stcg(p.x + e0 + i, v0[i]);
+                if (e0 + i < K) __stcg(p.x + e0 + i, v[i]);
         }
-        if (nw) {
+        if (norm) {
 #pragma unroll
-            for (int i = 0; i < 16; i++) v0[i] = __fmul_rn(__fmul_rn(v0[i], inv), w0[i]);
+            for (int i = 0; i < 16; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
         }
-        quant_block(q4, xq, xds, b, j, b < ph.nb, v0);
+        quant_block(q4, xq, xds, b, j, b < ph.nb, v);
     }
     named_sync(kBarConsumers, NCT);
 }
@@ -512,10 +618,10 @@ __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhas
     }
 }
 
-// one unit (a row, or a row pair when TWO) of a stage: this lane's blocks lane, lane + 32, ... (the first
+// one unit (a row, or a row pair when two) of a stage: this lane's blocks lane, lane + 32, ... (the first
 // XW from registers), summed over the warp
-template <int DT, bool TWO>
-__device__ __forceinline__ void unit_dot(const uint8_t *r0, int rbytes, int sbytes, int nb, const uint8_t *xq,
+template <int DT>
+__device__ __forceinline__ void unit_dot(bool two, const uint8_t *r0, int rbytes, int sbytes, int nb, const uint8_t *xq,
                                          const int2 *xds, const uint32_t (&xw)[XW][8], const float (&xd)[XW],
                                          const int (&xs)[XW], float &a0, float &a1) {
     const int lane = threadIdx.x & 31;
@@ -525,7 +631,7 @@ __device__ __forceinline__ void unit_dot(const uint8_t *r0, int rbytes, int sbyt
 #pragma unroll
         for (int c = 0; c < XW; c++) {
             a0 += dot_split<DT>(r0, sbytes, lane + 32 * c, xw[c], xd[c], xs[c]);
-            if (TWO) a1 += dot_split<DT>(r1, sbytes, lane + 32 * c, xw[c], xd[c], xs[c]);
+            if (two) a1 += dot_split<DT>(r1, sbytes, lane + 32 * c, xw[c], xd[c], xs[c]);
         }
         for (int b = lane + 32 * XW; b < nb; b += 32) {
             uint32_t xr[8];
@@ -533,7 +639,7 @@ __device__ __forceinline__ void unit_dot(const uint8_t *r0, int rbytes, int sbyt
             int rs;
             load_x(xq, xds, b, xr, rd, rs);
             a0 += dot_split<DT>(r0, sbytes, b, xr, rd, rs);
-            if (TWO) a1 += dot_split<DT>(r1, sbytes, b, xr, rd, rs);
+            if (two) a1 += dot_split<DT>(r1, sbytes, b, xr, rd, rs);
         }
     } else {
 #pragma unroll
@@ -541,30 +647,30 @@ __device__ __forceinline__ void unit_dot(const uint8_t *r0, int rbytes, int sbyt
             const int b = lane + 32 * c;
             if (b < nb) {
                 a0 += dot_split<DT>(r0, sbytes, b, xw[c], xd[c], xs[c]);
-                if (TWO) a1 += dot_split<DT>(r1, sbytes, b, xw[c], xd[c], xs[c]);
+                if (two) a1 += dot_split<DT>(r1, sbytes, b, xw[c], xd[c], xs[c]);
             }
         }
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-        if (TWO) a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+        if (two) a1 += __shfl_xor_sync(0xffffffffu, a1, o);
     }
 }
 
 // One matvec phase on this CTA's units.  Group grp takes the stages g with g % NG == grp; within the
-// group the units of its stages are dealt round-robin to its 4 warps, so a warp works alone: its own
+// group the units of its stages are dealt round-robin to its GW warps, so a warp works alone: its own
 // row dots and warp sums, and one arrival on each of its group's stages.  Epilogues are deferred: lane
 // k keeps the k-th pending unit's sums, and every 32 units (and at the end of the phase) all lanes run
 // their epilogues at once, their operand loads (RoPE pairs, residual x) in flight together.
-template <int DT, bool TWO>
-__device__ void run_matvec(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, uint64_t *full, uint64_t *empty,
-                           unsigned &gk, bool &dead, int pos, unsigned long long &best) {
+template <int DT>
+__device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, uint64_t *full, uint64_t *empty,
+                           unsigned &gk, bool &dead, int pos, unsigned long long &best, int phi) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, grp = warp / GW, wig = warp % GW;
     const uint8_t *xq = sm + p.off_xq;
     const int2 *xds = (const int2 *)(sm + p.off_xds);
     const int nb = ph.nb, sbytes = ph.sbytes, rbytes = ph.rbytes, R = ph.R;
-    constexpr int UR = TWO ? 2 : 1;
+    const int UR = two ? 2 : 1;
     uint32_t xw[XW][8];
     float xd[XW];
     int xs[XW];
@@ -586,38 +692,60 @@ __device__ void run_matvec(const DecodeParams &p, const DecodePhase &ph, uint8_t
     float pa0 = 0.0f, pa1 = 0.0f;  // this lane's pending unit: sums and index
     int64_t punit = 0;
     int npend = 0;  // pending units in the warp (warp-uniform)
+    unsigned long long twait = 0, tflush = 0, tdot = 0, nunits = 0;  // trace build only
     auto flush = [&]() {
+        const unsigned long long tf = trace_slot(phi, kTrFlush) ? clock64() : 0;
+        nunits += npend;
         if (lane < npend) {
             const float2 opnd = epilogue_operand(p, ph, punit, pos);
             epilogue(p, ph, punit, pa0, pa1, opnd, pos, best);
         }
         npend = 0;
+        if (trace_slot(phi, kTrFlush)) tflush += clock64() - tf;
     };
     for (int k = 0; k < nst; k++) {
         const unsigned g = gk + (unsigned)k;
         if ((int)(g % NG) != grp) continue;
         const int s = (int)(g % (unsigned)p.nslots);
+        const unsigned long long tw = trace_slot(phi, kTrFullWait) ? clock64() : 0;
+        if (lane == 0)
+            if (unsigned long long *q_ = trace_stage(p, g, 3))
+                *q_ = gtime() | (mbar_test(&full[s], (g / p.nslots) & 1u) ? (1ull << 63) : 0ull);
         if (!dead && !mbar_wait(&full[s], (g / p.nslots) & 1u)) {
             dead = true;
             if (lane == 0) raise_error(p.err, kErrMbarTimeout);
         }
+        if (trace_slot(phi, kTrFullWait)) twait += clock64() - tw;
+        if (lane == 0)
+            if (unsigned long long *q_ = trace_stage(p, g, 1)) *q_ = gtime();
         const int64_t ua = u0 + (int64_t)k * R;
         const int n = (int)min((int64_t)R, u1 - ua);
         const uint8_t *stage = sm + (size_t)s * p.slot_bytes;
         if (!dead) {
             for (int i = (wig - uoff % GW + GW) % GW; i < n; i += GW) {
                 float a0, a1;
-                unit_dot<DT, TWO>(stage + (int64_t)i * UR * rbytes, rbytes, sbytes, nb, xq, xds, xw, xd, xs, a0, a1);
+                const unsigned long long td = trace_slot(phi, kTrDot) ? clock64() : 0;
+                unit_dot<DT>(two, stage + (int64_t)i * UR * rbytes, rbytes, sbytes, nb, xq, xds, xw, xd, xs, a0, a1);
+                if (trace_slot(phi, kTrDot)) tdot += clock64() - td;
                 if (lane == npend) pa0 = a0, pa1 = a1, punit = ua + i;
                 if (++npend == 32) flush();
             }
         }
         uoff += n;
         __syncwarp();
+        if (lane == 0)
+            if (unsigned long long *q_ = trace_stage(p, g, 2)) *q_ = gtime_after(pa0 + pa1);
         if (lane == 0) mbar_arrive(&empty[s]);
     }
     if (!dead) flush();
     gk += (unsigned)nst;
+    if (lane == 0) {
+        DTRACE_ADD(phi, kTrFullWait, twait);
+        DTRACE_ADD(phi, kTrFlush, tflush);
+        DTRACE_ADD(phi, kTrDot, tdot);
+        DTRACE_ADD(phi, kTrUnits, nunits);
+        DTRACE_MAX(phi, kTrMvEnd, gtime());
+    }
 }
 
 // ---------------------------------------------------------------- attention phase
@@ -645,7 +773,7 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
             o[g][w] = 0.0f;
         }
     }
-    // positions t0 + warp, + 12, ...: the K and V rows of up to kAttnChunk of them are loaded at once
+    // positions t0 + warp, + NCW, ...: the K and V rows of up to kAttnChunk of them are loaded at once
     for (int tb = t0 + warp; tb < t1; tb += kAttnChunk * NCW) {
         float k[kAttnChunk][MAXW], v[kAttnChunk][MAXW];
 #pragma unroll
@@ -776,12 +904,11 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
         return;
     }
     if (warp == NCW) {  // producer warp: weights only, never waits on the consumers' barriers
-        if ((t & 31) == 0) producer(p, sm, full, empty);
+        producer(p, sm, full, empty);
         return;
     }
     unsigned gk = 0;
     bool dead = false;
-    unsigned long long best = 0;
     DecodePhase *dsm = (DecodePhase *)(sm + p.off_red + kRedDesc);
     desc_prefetch(p.ph, dsm);
     desc_wait();
@@ -792,20 +919,19 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
             if (!grid_sync(p, sm, (unsigned)i * gridDim.x, dead)) dead = true;
         }
         const DecodePhase &ph = dsm[i & 1];
+        if (t == 0) DTRACE_SET(i, kTrStart, gtime());
         if (i + 1 < p.nph) desc_prefetch(p.ph + i + 1, dsm + ((i + 1) & 1));
         if (ph.kind == PH_ATTN) {
             attention(p, ph, sm, pos);
+            if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
             continue;
         }
         prologue(p, ph, sm, token, pos);
+        if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
+        unsigned long long best = 0;  // this thread's argmax key (OUT phase)
         const bool two = ph.urows == 2;
-        if (ph.dtype == QMC_Q8_0) {
-            if (two) run_matvec<QMC_Q8_0, true>(p, ph, sm, full, empty, gk, dead, pos, best);
-            else run_matvec<QMC_Q8_0, false>(p, ph, sm, full, empty, gk, dead, pos, best);
-        } else {
-            if (two) run_matvec<QMC_Q4_0, true>(p, ph, sm, full, empty, gk, dead, pos, best);
-            else run_matvec<QMC_Q4_0, false>(p, ph, sm, full, empty, gk, dead, pos, best);
-        }
+        if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
+        else run_matvec<QMC_Q4_0>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
         if (ph.kind == PH_OUT) logits_argmax(p, sm, best);
     }
 }
@@ -839,6 +965,13 @@ int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, voi
     return QMC_OK;
 }
 
+#ifdef QMC_DECODE_TRACE
+// profiling build only: where the kernel writes its stamps ([phases][grid][kTrSlots] words; null: off)
+extern "C" __attribute__((visibility("default"))) int qmc_decode_trace_set(void *dev_buf) {
+    return (int)cudaMemcpyToSymbol(g_dtrace, &dev_buf, sizeof(dev_buf));
+}
+#endif
+
 bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out) {
     if (hd > 32 * MAXW) return false;
     auto r128 = [](int64_t b) { return (b + 127) / 128 * 128; };
@@ -846,19 +979,23 @@ bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t s
     const int64_t tree = r128((int64_t)(NCW / 2) * GMAX * (hd + 2) * 4);  // [warps handing over][GMAX][hd + 2]
     (void)group;
     const int64_t scratch = std::max(act, tree);
-    const int64_t fixed = 256 + scratch + kRedBytes;
-    const int64_t avail = (int64_t)smem_optin - fixed;
-    for (int ns : {5 * NG, 4 * NG, 3 * NG, 2 * NG, NG}) {
+    for (int ns : {2 * NG, NG}) {  // slots: a multiple of NG, so every slot belongs to one group
+        const int64_t bars = r128((int64_t)ns * 2 * 8);  // full[ns], empty[ns]
+        const int64_t avail = (int64_t)smem_optin - (bars + scratch + kRedBytes);
         const int64_t slot = (avail / ns) / 128 * 128;
         if (slot < max_unit_bytes) continue;
         DecodePlan d;
         d.nslots = ns;
+        d.groups = NG;
         d.slot_bytes = (int)slot;
         d.off_bars = (int)(ns * slot);
-        d.off_xq = d.off_bars + 256;
+        d.off_xq = d.off_bars + (int)bars;
         d.off_xds = d.off_xq + (int)r128((int64_t)nb_max * 32);
         d.off_red = d.off_xq + (int)scratch;
         d.smem = (size_t)d.off_red + kRedBytes;
+        if (d.off_xq < d.off_bars + ns * 16 || d.off_xds + (int64_t)nb_max * 8 > d.off_red ||
+            d.off_xq + tree > d.off_red || (int64_t)d.smem > (int64_t)smem_optin)
+            return false;  // regions overlap (cannot happen with the sizes above)
         *out = d;
         return true;
     }

@@ -64,6 +64,7 @@ struct DecodeParams {
 
 struct DecodePlan {
     int nslots = 0, slot_bytes = 0, off_bars = 0, off_xq = 0, off_xds = 0, off_red = 0;
+    int groups = 0;  // stage groups (consumer warps that each take every groups-th stage)
     size_t smem = 0;
 };
 // ring / shared-memory plan for the largest unit and activation length of the model; false if the

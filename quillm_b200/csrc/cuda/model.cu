@@ -247,8 +247,8 @@ int repack_weights(qmc_model *m) {
     return QMC_OK;
 }
 
-DecodePhase matrix_phase(const qmc_model *m, int kind, int dt, const uint8_t *W, int64_t units, int64_t K, int urows,
-                         const float *in, const float *norm_w, float *out) {
+DecodePhase matrix_phase(const qmc_model *m, int grid, int kind, int dt, const uint8_t *W, int64_t units, int64_t K,
+                         int urows, const float *in, const float *norm_w, float *out) {
     DecodePhase ph{};
     ph.kind = kind;
     ph.dtype = dt;
@@ -259,7 +259,16 @@ DecodePhase matrix_phase(const qmc_model *m, int kind, int dt, const uint8_t *W,
     ph.urows = urows;
     ph.rbytes = (int)split_row_bytes(dt, K);
     ph.sbytes = (int)split_scale_bytes(K);
-    ph.R = std::max(1, (int)(m->plan.slot_bytes / ((int64_t)urows * ph.rbytes)));
+    // units per stage: as many as a slot holds, or fewer when that evens out the busiest warp's share
+    // of the busiest CTA's units (ties: fewer, larger stages)
+    const int64_t rmax = std::max<int64_t>(1, m->plan.slot_bytes / ((int64_t)urows * ph.rbytes));
+    const int64_t per_cta = (units + grid - 1) / grid;
+    int64_t best = INT64_MAX;
+    for (int64_t r = 1; r <= rmax; r++) {
+        const int64_t stages = (per_cta + r - 1) / r;
+        const int64_t load = r * ((stages + m->plan.groups - 1) / m->plan.groups);  // units of the busiest warp
+        if (load <= best) best = load, ph.R = (int)r;
+    }
     ph.in = in;
     ph.norm_w = norm_w;
     ph.out = out;
@@ -276,7 +285,7 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
         for (int l = 0; l < m->L; l++) {
             Layer &Ly = m->layers[l];
             float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
-            DecodePhase qkv = matrix_phase(m, PH_QKV, Ly.dt[QMC_T_WQ], Ly.sqkv, (m->Dl + 2 * m->KVl) / 2, m->D, 2, m->x,
+            DecodePhase qkv = matrix_phase(m, c->num_sms, PH_QKV, Ly.dt[QMC_T_WQ], Ly.sqkv, (m->Dl + 2 * m->KVl) / 2, m->D, 2, m->x,
                                            Ly.attn_norm, nullptr);
             qkv.embed = l == 0;
             qkv.kc = kcl, qkv.vc = vcl;
@@ -285,11 +294,11 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
             at.kc = kcl, at.vc = vcl;
             m->phases.push_back(qkv);
             m->phases.push_back(at);
-            m->phases.push_back(matrix_phase(m, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x));
-            m->phases.push_back(matrix_phase(m, PH_FFN, Ly.dt[QMC_T_W1], Ly.s13, m->Hl, m->D, 2, m->x, Ly.ffn_norm, m->h));
-            m->phases.push_back(matrix_phase(m, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x));
+            m->phases.push_back(matrix_phase(m, c->num_sms, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x));
+            m->phases.push_back(matrix_phase(m, c->num_sms, PH_FFN, Ly.dt[QMC_T_W1], Ly.s13, m->Hl, m->D, 2, m->x, Ly.ffn_norm, m->h));
+            m->phases.push_back(matrix_phase(m, c->num_sms, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x));
         }
-        m->phases.push_back(matrix_phase(m, PH_OUT, m->dt_out, m->sout, m->Vl, m->D, 1, m->x, m->norm, m->logits));
+        m->phases.push_back(matrix_phase(m, c->num_sms, PH_OUT, m->dt_out, m->sout, m->Vl, m->D, 1, m->x, m->norm, m->logits));
         const int group = m->NH / m->NKV;
         m->gsplit = (group + kDecodeHeadsPerUnit - 1) / kDecodeHeadsPerUnit;
         m->maxseg = std::max(1, c->num_sms / (m->NKVl * m->gsplit));
