@@ -703,9 +703,8 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         npend = 0;
         if (trace_slot(phi, kTrFlush)) tflush += clock64() - tf;
     };
-    for (int k = 0; k < nst; k++) {
+    for (int k = (int)((unsigned)(grp + NG) - gk % NG) % NG; k < nst; k += NG) {  // this group's stages
         const unsigned g = gk + (unsigned)k;
-        if ((int)(g % NG) != grp) continue;
         const int s = (int)(g % (unsigned)p.nslots);
         const unsigned long long tw = trace_slot(phi, kTrFullWait) ? clock64() : 0;
         if (lane == 0)
