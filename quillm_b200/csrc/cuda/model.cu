@@ -259,16 +259,21 @@ DecodePhase matrix_phase(const qmc_model *m, int grid, int kind, int dt, const u
     ph.urows = urows;
     ph.rbytes = (int)split_row_bytes(dt, K);
     ph.sbytes = (int)split_scale_bytes(K);
-    // units per stage: as many as a slot holds, or fewer when that evens out the busiest warp's share
-    // of the busiest CTA's units (ties: fewer, larger stages)
+    // units per stage: the most a slot holds (more bytes in flight per warp) unless fewer evens out the
+    // busiest warp's share of the busiest CTA's units by more than ~15 %
     const int64_t rmax = std::max<int64_t>(1, m->plan.slot_bytes / ((int64_t)urows * ph.rbytes));
     const int64_t per_cta = (units + grid - 1) / grid;
-    int64_t best = INT64_MAX;
-    for (int64_t r = 1; r <= rmax; r++) {
+    auto load = [&](int64_t r) {  // units of the busiest warp
         const int64_t stages = (per_cta + r - 1) / r;
-        const int64_t load = r * ((stages + m->plan.groups - 1) / m->plan.groups);  // units of the busiest warp
-        if (load <= best) best = load, ph.R = (int)r;
-    }
+        return r * ((stages + m->plan.groups - 1) / m->plan.groups);
+    };
+    int64_t best = INT64_MAX;
+    for (int64_t r = 1; r <= rmax; r++) best = std::min(best, load(r));
+    for (int64_t r = rmax; r >= 1; r--)
+        if (load(r) * 100 <= best * 115) {
+            ph.R = (int)r;
+            break;
+        }
     ph.in = in;
     ph.norm_w = norm_w;
     ph.out = out;
