@@ -130,6 +130,14 @@ int qmc_model_synthesize(qmc_model *m, int dtype, uint64_t seed, double std);
 /* one decode step for (token, pos).  logits_host (optional, vocab floats) receives the logits;
  * next_token (optional) receives the greedy argmax.  Returns QMC_EINVAL on a bad token or pos. */
 int qmc_model_forward(qmc_model *m, int32_t token, int32_t pos, float *logits_host, int32_t *next_token);
+/* batched prompt forward: tokens[0..n) at positions pos0 .. pos0+n-1 through every layer together (each
+ * matrix applied once to all n rows), filling those KV-cache slots; logits_host / next_token receive the
+ * last token's logits and greedy argmax, as qmc_model_forward at pos0+n-1 would after feeding the prompt
+ * one token at a time.  Replaces the reference's token-at-a-time prompt loop (src/main.c:129); single-GPU
+ * models only (QMC_EINVAL under tensor parallelism).  Row buffers for n tokens are allocated on the first
+ * call that needs them. */
+int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t pos0, float *logits_host,
+                      int32_t *next_token);
 /* greedy generation kept on the device: feeds prompt[0..n_prompt) one token per step from position 0,
  * then appends n_gen greedy tokens; one host synchronisation at the end.  out_tokens gets n_gen ids. */
 int qmc_model_generate(qmc_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen, int32_t *out_tokens);

@@ -94,6 +94,7 @@ _CUDA_SIGS = {
     "qmc_model_synthesize": (I, [V, I, C.c_uint64, D]),
     "qmc_model_forward": (I, [V, I32, I32, P, P]),
     "qmc_model_generate": (I, [V, P, I32, I32, P]),
+    "qmc_model_prefill": (I, [V, P, I32, I32, P, P]),
     "qmc_model_enqueue_decode": (I, [V, I32, I32, I32]),
     "qmc_model_state": (I, [V, C.POINTER(I32), C.POINTER(I32)]),
     "qmc_model_logits": (I, [V, C.POINTER(V)]),
@@ -142,6 +143,7 @@ _HOST_SIGS = {
     "qm_model_free": (None, [C.POINTER(QmModel)]),
     "qm_model_forward": (C.POINTER(C.c_float), [C.POINTER(QmModel), I32, I32]),
     "qm_model_generate": (I, [C.POINTER(QmModel), P, I32, I32, P]),
+    "qm_model_prefill": (C.POINTER(C.c_float), [C.POINTER(QmModel), P, I32, I32]),
 }
 
 
@@ -215,6 +217,17 @@ class Model:
         nxt = C.c_int32(0)
         check(self.lib.qmc_model_forward(self.h, token, pos, None if logits is None else logits.ctypes.data,
                                          C.byref(nxt)), "model_forward")
+        return nxt.value
+
+    def prefill(self, tokens, pos0: int = 0, logits=None) -> int:
+        """the prompt's tokens through every layer at once (KV slots pos0 .. pos0+len-1); returns the
+        last token's greedy argmax and fills `logits` (float32[vocab]) when given"""
+        import numpy as np
+
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = C.c_int32(0)
+        check(self.lib.qmc_model_prefill(self.h, t.ctypes.data, len(t), pos0,
+                                         None if logits is None else logits.ctypes.data, C.byref(nxt)), "model_prefill")
         return nxt.value
 
     def generate(self, prompt, n_gen: int):

@@ -44,6 +44,21 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// dequantized value of element c of a row (src/quant.c:65-94): fp32(d) * (float)q, one rounding
+__device__ __forceinline__ float deq_elem(int dtype, const uint8_t *row, int64_t c) {
+    if (dtype == QMC_F32) return ((const float *)row)[c];
+    const int64_t b = c >> 5;
+    const int k = (int)(c & 31);
+    if (dtype == QMC_Q8_0) {
+        const uint8_t *blk = row + b * kQ8Bytes;
+        return h2f(blk[0] | (blk[1] << 8)) * (float)(int8_t)blk[2 + k];
+    }
+    const uint8_t *blk = row + b * kQ4Bytes;
+    const int byte = blk[2 + (k >> 1)];
+    const int q = (k & 1) ? (byte >> 4) : (byte & 15);
+    return h2f(blk[0] | (blk[1] << 8)) * (float)(q - 8);
+}
+
 // ---------------------------------------------------------------- block quantization (warp per block)
 // Lane i holds element i of a 32-element block (0 for the zero-padded tail).  Every lane returns
 // its quantized value; *dd receives fp32(fp16(amax / qmax)) and *dh its fp16 bits.  Bit-exact with

@@ -31,21 +31,6 @@ __global__ void quantize_rows_kernel(int dtype, const float *__restrict__ x, uin
     }
 }
 
-// dequantized value of element c of a row (src/quant.c:65-94): fp32(d) * (float)q, one rounding
-__device__ __forceinline__ float deq_elem(int dtype, const uint8_t *row, int64_t c) {
-    if (dtype == QMC_F32) return ((const float *)row)[c];
-    const int64_t b = c >> 5;
-    const int k = (int)(c & 31);
-    if (dtype == QMC_Q8_0) {
-        const uint8_t *blk = row + b * kQ8Bytes;
-        return h2f(blk[0] | (blk[1] << 8)) * (float)(int8_t)blk[2 + k];
-    }
-    const uint8_t *blk = row + b * kQ4Bytes;
-    const int byte = blk[2 + (k >> 1)];
-    const int q = (k & 1) ? (byte >> 4) : (byte & 15);
-    return h2f(blk[0] | (blk[1] << 8)) * (float)(q - 8);
-}
-
 __global__ void dequantize_rows_kernel(int dtype, const uint8_t *__restrict__ in, float *__restrict__ y, int64_t rows,
                                        int64_t cols) {
     const int64_t rb = row_bytes(dtype, cols);

@@ -23,6 +23,8 @@
 #include "decode.cuh"
 #include "elementwise.cuh"
 #include "gemv.cuh"
+#include "matmul.cuh"
+#include "prefill.cuh"
 #include "synth.cuh"
 
 using namespace qmc;
@@ -68,6 +70,12 @@ struct qmc_model {
     unsigned *gbar = nullptr;
     float *apart = nullptr;
     int maxseg = 1, gsplit = 1;
+    // batched prompt forward: row buffers for up to pf_cap tokens (allocated on first use, grown on demand)
+    int pf_cap = 0;
+    int *pf_tok = nullptr;
+    float *pf_x = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_c = nullptr, *pf_h = nullptr,
+          *pf_h3 = nullptr, *pf_ad = nullptr;
+    int8_t *pf_aq = nullptr;
 };
 
 namespace {
@@ -626,6 +634,94 @@ int qmc_model_forward(qmc_model *m, int32_t token, int32_t pos, float *logits_ho
     RC(step_status(m));
     if (logits_host) memcpy(logits_host, m->h_logits, (size_t)m->V * 4);
     if (next_token) *next_token = m->h_state[4];
+    return QMC_OK;
+}
+
+namespace {
+// row buffers for T prompt tokens (old buffers stay allocated until the model is freed)
+int prefill_buffers(qmc_model *m, int T) {
+    if (T <= m->pf_cap) return QMC_OK;
+    const int cap = std::min(m->S, std::max(T, ((T + 63) / 64) * 64));
+    const int64_t wide = std::max<int64_t>(m->D, std::max<int64_t>(m->Hl, m->Dl + 2 * m->KVl));
+    const int64_t nbk = nblocks(std::max<int64_t>(m->D, std::max<int64_t>(m->Hl, m->Dl)));
+    int rc;
+    if ((rc = dalloc(m, (void **)&m->pf_tok, (size_t)cap * 4)) || (rc = dalloc(m, (void **)&m->pf_x, (size_t)cap * m->D * 4)) ||
+        (rc = dalloc(m, (void **)&m->pf_xn, (size_t)cap * m->D * 4)) ||
+        (rc = dalloc(m, (void **)&m->pf_qkv, (size_t)cap * (m->Dl + 2 * m->KVl) * 4)) ||
+        (rc = dalloc(m, (void **)&m->pf_att, (size_t)cap * m->Dl * 4)) || (rc = dalloc(m, (void **)&m->pf_c, (size_t)cap * wide * 4)) ||
+        (rc = dalloc(m, (void **)&m->pf_h, (size_t)cap * m->Hl * 4)) || (rc = dalloc(m, (void **)&m->pf_h3, (size_t)cap * m->Hl * 4)) ||
+        (rc = dalloc(m, (void **)&m->pf_aq, (size_t)cap * nbk * 32)) || (rc = dalloc(m, (void **)&m->pf_ad, (size_t)cap * nbk * 4)))
+        return rc;
+    m->pf_cap = cap;
+    return QMC_OK;
+}
+
+// C[T][N] = A[T][K] . W^T: quantized W through per-row Q8_0 activations (row t = the matvec of A[t],
+// src/ops.c:57-61), f32 W as the f32 contraction
+int prefill_proj(qmc_model *m, int dt, const void *W, const float *A, int T, int64_t N, int64_t K, float *C) {
+    if (dt == QMC_F32) return launch_gemm_f32(A, (const float *)W, C, T, N, K, m->stream);
+    RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream));
+    return launch_matmul_q(dt, W, m->pf_aq, m->pf_ad, C, T, N, K, m->stream);
+}
+}  // namespace
+
+int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t pos0, float *logits_host,
+                      int32_t *next_token) {
+    if (!m || !tokens || n < 1 || pos0 < 0 || (int64_t)pos0 + n > m->S)
+        return set_error(QMC_EINVAL, "prefill: bad arguments (n %d, pos0 %d, max_seq %d)", n, pos0, m ? m->S : 0);
+    if (m->tp != 1) return set_error(QMC_EINVAL, "prefill: tensor-parallel models decode the prompt token by token");
+    for (int i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= m->V) return set_error(QMC_EINVAL, "prefill: token %d out of range", tokens[i]);
+    RC(check_dev(m));
+    RC(prefill_buffers(m, n));
+    cudaStream_t s = m->stream;
+    DevCtx *c = ctx();
+    const int D = m->D, Dq = m->Dl, KVl = m->KVl, H = m->Hl, NQKV = Dq + 2 * KVl;
+    const float eps = m->cfg.norm_eps;
+    QMC_CUDA(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    RC(launch_embed_rows(m->dt_tok, m->tok, D, m->pf_tok, n, m->pf_x, s));
+    const int64_t kvstride = (int64_t)m->S * KVl;
+    for (int l = 0; l < m->L; l++) {
+        Layer &Ly = m->layers[l];
+        float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
+        RC(launch_rmsnorm_rows(m->pf_x, Ly.attn_norm, m->pf_xn, n, D, eps, s));
+        RC(prefill_proj(m, Ly.dt[QMC_T_WQ], Ly.wqkv, m->pf_xn, n, NQKV, D, m->pf_qkv));
+        RC(launch_rope_kv_rows(m->pf_qkv, n, Dq, KVl, m->hd, pos0, m->rope, kcl, vcl, s));
+        RC(launch_attn_prefill(m->pf_qkv, n, NQKV, m->NHl, m->NH / m->NKV, m->hd, KVl, pos0, 1.0f / sqrtf((float)m->hd), kcl,
+                               vcl, m->pf_att, s));
+        RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
+        RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
+        RC(launch_rmsnorm_rows(m->pf_x, Ly.ffn_norm, m->pf_xn, n, D, eps, s));
+        RC(prefill_proj(m, Ly.dt[QMC_T_W1], Ly.w1, m->pf_xn, n, H, D, m->pf_h));
+        RC(prefill_proj(m, Ly.dt[QMC_T_W3], Ly.w3, m->pf_xn, n, H, D, m->pf_h3));
+        RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
+        RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
+        RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
+    }
+    // logits of the last token: the output GEMV with the final rmsnorm fused, as a decode step's
+    GemvArgs g;
+    g.dtype = m->dt_out;
+    g.W0 = m->out;
+    g.rows = m->Vl;
+    g.K = D;
+    g.x = m->pf_x + (int64_t)(n - 1) * D;
+    g.norm_w = m->norm;
+    g.eps = eps;
+    g.y = m->logits;
+    g.epi = EPI_STORE;
+    g.err = c->err;
+    RC(launch_gemv(g, s, false));
+    QMC_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s));
+    QMC_CUDA(cudaStreamSynchronize(s));
+    RC(qmc_check_device_error());
+    if (logits_host) memcpy(logits_host, m->h_logits, (size_t)m->V * 4);
+    if (next_token) {  // first maximum; a NaN in slot 0 is never replaced (src/sampler.c:27-32)
+        int bi = 0;
+        float bv = m->h_logits[0];
+        for (int i = 1; i < m->V; i++)
+            if (m->h_logits[i] > bv) bv = m->h_logits[i], bi = i;
+        *next_token = bi;
+    }
     return QMC_OK;
 }
 

@@ -152,6 +152,15 @@ float *qm_model_forward(qm_model *m, int32_t token, int32_t pos) {
     return m->logits;
 }
 
+float *qm_model_prefill(qm_model *m, const int32_t *tokens, int32_t n, int32_t pos0) {
+    if (!tokens || n < 1 || pos0 < 0 || (int64_t)pos0 + n > m->cfg.max_seq) return NULL;
+    if (qmc_model_prefill(m->gpu, tokens, n, pos0, m->logits, NULL) != QMC_OK) {
+        qh_fail("qm_model_prefill");
+        return NULL;
+    }
+    return m->logits;
+}
+
 int qm_model_generate(qm_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen, int32_t *out_tokens) {
     if (qmc_model_generate(m->gpu, prompt, n_prompt, n_gen, out_tokens) != QMC_OK) {
         qh_fail("qm_model_generate");
