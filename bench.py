@@ -337,6 +337,17 @@ def gpu_arm(args, wl: dict) -> dict | None:
         t = model.forward(t, pos + 1 + i, logits)
     e2e_s = d.max(time.perf_counter() - t0)
 
+    # sampled decoding through the public call: temperature 0.8 / top-p 0.9 drawn on the device, only the
+    # 4-byte token copied back per step (the reference's loop copies the logits and samples on the host)
+    sampler = qb.Sampler(cfg["vocab_size"], 0.8, 0, 0.9, 1234)
+    t = model.forward_sample(tok, pos, sampler)  # warm
+    d.barrier()
+    t0 = time.perf_counter()
+    for i in range(K):
+        t = model.forward_sample(t, pos + 1 + i, sampler)
+    e2e_sampled_s = d.max(time.perf_counter() - t0)
+    sampler.close()
+
     # batched prompt forward (single GPU): the same prompt through every layer at once, timed through
     # the public call (host token copy in, logits copy out, one synchronisation)
     prefill = None
@@ -377,6 +388,8 @@ def gpu_arm(args, wl: dict) -> dict | None:
         "prefill": prefill,
         "e2e": {"value": K / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": cfg["vocab_size"] * 4 + 4},
+        "e2e_sampled": {"value": K / e2e_sampled_s, "unit": "tok/s", "sampling": "temperature 0.8, top-p 0.9, on the device",
+                        "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
         "gpu_launches": K * launches,
         "clocks": clk,
     }

@@ -158,6 +158,29 @@ int qmc_model_step_bytes(const qmc_model *m, int32_t pos, double *bytes);
 int qmc_model_decode_info(const qmc_model *m, int32_t *launches, int32_t *persistent);
 int qmc_model_free(qmc_model *m);
 
+/* ---- device-side sampler: temperature / top-k / top-p with the reference's xorshift64* stream
+ * (src/sampler.c qm_sampler_init / qm_sample / qm_rng_uniform), drawing from logits in device memory so
+ * a decode loop copies back one token instead of the vocab's logits.  Same candidate ranking, nucleus
+ * and draw as the reference; probabilities use the device expf and sums run in another order, so a draw
+ * can differ only where u falls within rounding of a cumulative-mass boundary. */
+typedef struct qmc_sampler qmc_sampler;
+/* settings normalised as qm_sampler_init (src/sampler.c:6-16): temperature < 0 -> 0 (greedy), top_k < 0
+ * -> 0 (off), top_p outside (0, 1] -> 1 (off), seed 0 -> the reference's fixed default; allocates its
+ * state and n_vocab floats of scratch on the current device */
+int qmc_sampler_create(int32_t n_vocab, float temperature, int32_t top_k, float top_p, uint64_t seed,
+                       qmc_sampler **out);
+/* one draw from dev_logits[n_vocab] into *dev_token, enqueued on `stream` (NULL: the thread's stream);
+ * the RNG state advances on the device in stream order */
+int qmc_sampler_enqueue(qmc_sampler *s, const float *dev_logits, int32_t *dev_token, void *stream);
+/* one draw, synchronously, into *token (host) */
+int qmc_sampler_sample(qmc_sampler *s, const float *dev_logits, int32_t *token);
+/* the current xorshift64* state (synchronises the device) */
+int qmc_sampler_rng(qmc_sampler *s, uint64_t *state);
+int qmc_sampler_free(qmc_sampler *s);
+/* one decode step for (token, pos) whose next token is drawn by the sampler on the device: only the
+ * 4-byte token comes back (qm_model_forward + qm_sample of src/main.c without the logits copy) */
+int qmc_model_forward_sample(qmc_model *m, int32_t token, int32_t pos, qmc_sampler *s, int32_t *next_token);
+
 #pragma GCC visibility pop
 #ifdef __cplusplus
 }

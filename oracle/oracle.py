@@ -87,12 +87,42 @@ def ref():
             "ref_decode_time": (D, [V, I32, I32, I, V]),
             "qm_rmsnorm": (None, [V, V, V, I64, F]), "qm_softmax": (None, [V, I64]),
             "qm_rope": (None, [V, I64, I64, I64, F]), "qm_swiglu": (None, [V, V, I64]),
+            "qm_sample": (I32, [V, V]), "qm_rng_uniform": (F, [V]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(lib, n)
             fn.restype, fn.argtypes = r, a
         _ref = lib
     return _ref
+
+
+class _QmSampler(C.Structure):
+    """the reference's qm_sampler (src/sampler.h:8-16)"""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float), ("rng", C.c_uint64),
+                ("n_vocab", C.c_int32), ("probs", C.POINTER(C.c_float)), ("idx", C.POINTER(C.c_int32))]
+
+
+class RefSampler:
+    """The reference's own qm_sample (src/sampler.c) on host logits, its settings normalised as
+    qm_sampler_init does (src/sampler.c:6-16) with the scratch owned here instead of an arena."""
+
+    def __init__(self, n_vocab: int, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0):
+        import numpy as np
+        self.lib = ref()
+        self._probs = np.zeros(n_vocab, np.float32)
+        self._idx = np.zeros(n_vocab, np.int32)
+        self.s = _QmSampler(max(temperature, 0.0), max(top_k, 0), 1.0 if (top_p <= 0 or top_p > 1) else top_p,
+                            seed or 0x9E3779B97F4A7C15, n_vocab,
+                            self._probs.ctypes.data_as(C.POINTER(C.c_float)), self._idx.ctypes.data_as(C.POINTER(C.c_int32)))
+
+    def sample(self, logits) -> int:
+        import numpy as np
+        lg = np.ascontiguousarray(logits, np.float32)
+        return int(self.lib.qm_sample(C.byref(self.s), lg.ctypes.data))
+
+    @property
+    def rng(self) -> int:
+        return int(self.s.rng)
 
 
 # ------------------------------------------------------------------ numpy conveniences

@@ -102,6 +102,12 @@ _CUDA_SIGS = {
     "qmc_model_step_bytes": (I, [V, I32, C.POINTER(D)]),
     "qmc_model_decode_info": (I, [V, C.POINTER(I32), C.POINTER(I32)]),
     "qmc_model_free": (I, [V]),
+    "qmc_sampler_create": (I, [I32, F, I32, F, C.c_uint64, P]),
+    "qmc_sampler_enqueue": (I, [V, P, P, V]),
+    "qmc_sampler_sample": (I, [V, P, P]),
+    "qmc_sampler_rng": (I, [V, P]),
+    "qmc_sampler_free": (I, [V]),
+    "qmc_model_forward_sample": (I, [V, I32, I32, V, P]),
 }
 
 _HOST_SIGS = {
@@ -195,6 +201,31 @@ def ptr(t) -> int:
     return t.ctypes.data
 
 
+class Sampler:
+    """device-side sampler (temperature / top-k / top-p, the reference's xorshift64* stream)"""
+
+    def __init__(self, n_vocab: int, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0):
+        self.lib = cuda()
+        self.h = C.c_void_p()
+        check(self.lib.qmc_sampler_create(n_vocab, temperature, top_k, top_p, seed, C.byref(self.h)), "sampler_create")
+
+    def sample(self, dev_logits: int) -> int:
+        """one draw from float32 logits at device address dev_logits"""
+        t = C.c_int32(0)
+        check(self.lib.qmc_sampler_sample(self.h, C.c_void_p(dev_logits), C.byref(t)), "sampler_sample")
+        return t.value
+
+    def rng(self) -> int:
+        st = C.c_uint64(0)
+        check(self.lib.qmc_sampler_rng(self.h, C.byref(st)), "sampler_rng")
+        return st.value
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.qmc_sampler_free(self.h)
+            self.h = C.c_void_p()
+
+
 class Model:
     """A libquillm_cuda model (qmc_model*) on the current device."""
 
@@ -217,6 +248,12 @@ class Model:
         nxt = C.c_int32(0)
         check(self.lib.qmc_model_forward(self.h, token, pos, None if logits is None else logits.ctypes.data,
                                          C.byref(nxt)), "model_forward")
+        return nxt.value
+
+    def forward_sample(self, token: int, pos: int, sampler: "Sampler") -> int:
+        """one decode step whose next token the sampler draws on the device"""
+        nxt = C.c_int32(0)
+        check(self.lib.qmc_model_forward_sample(self.h, token, pos, sampler.h, C.byref(nxt)), "model_forward_sample")
         return nxt.value
 
     def prefill(self, tokens, pos0: int = 0, logits=None) -> int:

@@ -53,7 +53,7 @@ struct qmc_model {
     float *x = nullptr, *xb = nullptr, *q = nullptr, *h = nullptr, *logits_l = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr, *attn_part = nullptr;
     float2 *rope = nullptr;
-    int *state = nullptr;  // [0] token  [1] pos  [2] step  [3] prompt length
+    int *state = nullptr;  // [0] token  [1] pos  [2] step  [3] prompt length  [8] sampled token
     int *forced = nullptr, *gen = nullptr, *attn_cnt = nullptr;
     unsigned long long *amax = nullptr;  // [0] argmax key, [1] low 32 bits: CTA ticket (fused output argmax)
     int *h_state = nullptr;
@@ -541,7 +541,7 @@ int qmc_model_create(const qmc_config *cfg, int tp_rank, int tp_size, const void
         (rc = dalloc(m, (void **)&m->logits, (size_t)m->V * 4)) || (rc = dalloc(m, (void **)&m->kc, kvbytes)) ||
         (rc = dalloc(m, (void **)&m->vc, kvbytes)) || (rc = dalloc(m, (void **)&m->attn_part, m->ap.part_floats * 4)) ||
         (rc = dalloc(m, (void **)&m->attn_cnt, (size_t)m->NKVl * 4)) ||
-        (rc = dalloc(m, (void **)&m->rope, (size_t)m->S * (hd / 2) * 8)) || (rc = dalloc(m, (void **)&m->state, 16)) ||
+        (rc = dalloc(m, (void **)&m->rope, (size_t)m->S * (hd / 2) * 8)) || (rc = dalloc(m, (void **)&m->state, 64)) ||
         (rc = dalloc(m, (void **)&m->forced, (size_t)m->S * 4)) || (rc = dalloc(m, (void **)&m->gen, (size_t)m->S * 4)) ||
         (rc = dalloc(m, (void **)&m->amax, 16)))
         return fail(rc);
@@ -722,6 +722,23 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
             if (m->h_logits[i] > bv) bv = m->h_logits[i], bi = i;
         *next_token = bi;
     }
+    return QMC_OK;
+}
+
+int qmc_model_forward_sample(qmc_model *m, int32_t token, int32_t pos, qmc_sampler *s, int32_t *next_token) {
+    if (!m || !s || !next_token) return set_error(QMC_EINVAL, "forward_sample: null argument");
+    if (token < 0 || token >= m->V || pos < 0 || pos >= m->S)
+        return set_error(QMC_EINVAL, "forward_sample: token %d / pos %d out of range", token, pos);
+    RC(check_dev(m));
+    RC(build_graph(m));
+    m->h_state[0] = token, m->h_state[1] = pos, m->h_state[2] = 0, m->h_state[3] = 0;
+    QMC_CUDA(cudaMemcpyAsync(m->state, m->h_state, 16, cudaMemcpyHostToDevice, m->stream));
+    QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
+    RC(qmc_sampler_enqueue(s, m->logits, m->state + 8, m->stream));
+    QMC_CUDA(cudaMemcpyAsync(m->h_state + 4, m->state + 8, 4, cudaMemcpyDeviceToHost, m->stream));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    RC(step_status(m));
+    *next_token = m->h_state[4];
     return QMC_OK;
 }
 
