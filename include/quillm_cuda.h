@@ -51,6 +51,12 @@ int qmc_sync(void);
 int qmc_check_device_error(void);
 
 /* ---- device buffers (for host layers that own no CUDA code) ---- */
+/* page-lock [ptr, ptr + bytes) of host memory (read-only mappings allowed, e.g. a mapped .qlm) so that
+ * qmc_model_upload / qmc_upload_tensor copy from it by DMA without a staging copy; undo with
+ * qmc_host_unregister before the memory goes away.  The loaders in libquillm do this around their
+ * uploads (replaces the reference's mmap-only load, src/qlm_file.c:152-172). */
+int qmc_host_register(const void *ptr, size_t bytes);
+int qmc_host_unregister(const void *ptr);
 int qmc_malloc(void **dptr, size_t bytes);
 int qmc_free(void *dptr);
 int qmc_memcpy_h2d(void *dst, const void *src, size_t bytes, void *stream);

@@ -91,6 +91,8 @@ _CUDA_SIGS = {
     "qmc_nccl_unique_id": (I, [V]),
     "qmc_model_create": (I, [C.POINTER(QmcConfig), I, I, V, C.POINTER(V)]),
     "qmc_model_upload": (I, [V, I, I, I, I64, I64, V]),
+    "qmc_host_register": (I, [V, S]),
+    "qmc_host_unregister": (I, [V]),
     "qmc_model_synthesize": (I, [V, I, C.c_uint64, D]),
     "qmc_model_forward": (I, [V, I32, I32, P, P]),
     "qmc_model_generate": (I, [V, P, I32, I32, P]),
@@ -320,13 +322,19 @@ def load_qlm_into(model: Model, path: str) -> None:
         for l in range(L):
             for k, v in per.items():
                 kinds[f"layers.{l}.{k}"] = (v, l)
-        for i in range(f.n_tensors):
-            t = f.tensors[i]
-            name = t.name.decode()
-            if name not in kinds:
-                continue
-            kind, layer = kinds[name]
-            cols = t.ne[1] if t.ndim == 2 else 0
-            check(model.lib.qmc_model_upload(model.h, kind, layer, t.type, t.ne[0], cols, t.data), f"upload {name}")
+        # page-lock the mapping for the uploads: DMA straight from the file's pages
+        pinned = model.lib.qmc_host_register(f.map, f.map_size) == 0
+        try:
+            for i in range(f.n_tensors):
+                t = f.tensors[i]
+                name = t.name.decode()
+                if name not in kinds:
+                    continue
+                kind, layer = kinds[name]
+                cols = t.ne[1] if t.ndim == 2 else 0
+                check(model.lib.qmc_model_upload(model.h, kind, layer, t.type, t.ne[0], cols, t.data), f"upload {name}")
+        finally:
+            if pinned:
+                model.lib.qmc_host_unregister(f.map)
     finally:
         h.qlm_close(C.byref(f))

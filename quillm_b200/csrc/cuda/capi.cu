@@ -147,6 +147,19 @@ int qmc_check_device_error(void) {
     return QMC_OK;
 }
 
+int qmc_host_register(const void *ptr, size_t bytes) {
+    if (!ptr || !bytes) return set_error(QMC_EINVAL, "host_register: null range");
+    // read-only and portable: a loader's read-only file mapping qualifies, every device may DMA from it
+    QMC_CUDA(cudaHostRegister(const_cast<void *>(ptr), bytes, cudaHostRegisterReadOnly | cudaHostRegisterPortable));
+    return QMC_OK;
+}
+
+int qmc_host_unregister(const void *ptr) {
+    if (!ptr) return set_error(QMC_EINVAL, "host_unregister: null pointer");
+    QMC_CUDA(cudaHostUnregister(const_cast<void *>(ptr)));
+    return QMC_OK;
+}
+
 int qmc_malloc(void **dptr, size_t bytes) {
     CTX_OR_FAIL();
     QMC_CUDA(cudaMalloc(dptr, bytes ? bytes : 1));

@@ -100,18 +100,22 @@ static int load_common(qm_model *m, const char *path, int n_threads, int max_seq
         snprintf(err, errlen, "device model: %s", qmc_last_error());
         goto fail;
     }
-    if (upload(m, QMC_T_TOK_EMBD, -1, m->tok_embd, err, errlen) || upload(m, QMC_T_NORM, -1, m->norm, err, errlen) ||
-        upload(m, QMC_T_OUTPUT, -1, m->output, err, errlen))
-        goto fail;
+    /* page-lock the mapped file for the uploads so every tensor goes to HBM by DMA straight from the
+     * mapping (no staging copy); without it (registration refused) the uploads still work, slower */
+    const int pinned = qmc_host_register(f->map, f->map_size) == QMC_OK;
+    if (!pinned) qmc_last_error();
+    int up_rc = upload(m, QMC_T_TOK_EMBD, -1, m->tok_embd, err, errlen) || upload(m, QMC_T_NORM, -1, m->norm, err, errlen) ||
+                upload(m, QMC_T_OUTPUT, -1, m->output, err, errlen);
     static const int kinds[9] = {QMC_T_ATTN_NORM, QMC_T_WQ, QMC_T_WK, QMC_T_WV, QMC_T_WO,
                                  QMC_T_FFN_NORM,  QMC_T_W1, QMC_T_W2, QMC_T_W3};
-    for (int l = 0; l < c->n_layers; l++) {
+    for (int l = 0; l < c->n_layers && !up_rc; l++) {
         const qm_tensor *ts[9] = {m->layers[l].attn_norm, m->layers[l].wq, m->layers[l].wk,
                                   m->layers[l].wv,        m->layers[l].wo, m->layers[l].ffn_norm,
                                   m->layers[l].w1,        m->layers[l].w2, m->layers[l].w3};
-        for (int k = 0; k < 9; k++)
-            if (upload(m, kinds[k], l, ts[k], err, errlen)) goto fail;
+        for (int k = 0; k < 9 && !up_rc; k++) up_rc = upload(m, kinds[k], l, ts[k], err, errlen);
     }
+    if (pinned) qmc_host_unregister(f->map);
+    if (up_rc) goto fail;
     if (qm_arena_init(&m->arena, (size_t)V * 4 + QM_ALIGN) != 0 || !(m->logits = qm_arena_alloc(&m->arena, (size_t)V * 4))) {
         snprintf(err, errlen, "out of memory for runtime state");
         goto fail;
