@@ -693,17 +693,27 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
     int64_t punit = 0;
     int npend = 0;  // pending units in the warp (warp-uniform)
     unsigned long long twait = 0, tflush = 0, tdot = 0, nunits = 0;  // trace build only
+    const int k0 = (int)((unsigned)(grp + NG) - gk % NG) % NG;  // this group's first stage of the phase
+    // the first 32 units this warp will compute are known now: lane l loads unit l's epilogue operand
+    // (RoPE pair, residual x) before the first stage, so the last flush does not wait on L2
+    float2 opre = make_float2(0.0f, 0.0f);
+    {
+        const int64_t k = k0 + (int64_t)(lane / R) * NG, unit = u0 + k * R + lane % R;
+        if (GW == 1 && k < nst && unit < u1) opre = epilogue_operand(p, ph, unit, pos);
+    }
+    bool first_batch = GW == 1;
     auto flush = [&]() {
         const unsigned long long tf = trace_slot(phi, kTrFlush) ? clock64() : 0;
         nunits += npend;
         if (lane < npend) {
-            const float2 opnd = epilogue_operand(p, ph, punit, pos);
+            const float2 opnd = first_batch ? opre : epilogue_operand(p, ph, punit, pos);
             epilogue(p, ph, punit, pa0, pa1, opnd, pos, best);
         }
         npend = 0;
+        first_batch = false;
         if (trace_slot(phi, kTrFlush)) tflush += clock64() - tf;
     };
-    for (int k = (int)((unsigned)(grp + NG) - gk % NG) % NG; k < nst; k += NG) {  // this group's stages
+    for (int k = k0; k < nst; k += NG) {  // this group's stages
         const unsigned g = gk + (unsigned)k;
         const int s = (int)(g % (unsigned)p.nslots);
         const unsigned long long tw = trace_slot(phi, kTrFullWait) ? clock64() : 0;
