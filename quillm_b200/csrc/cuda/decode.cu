@@ -7,11 +7,12 @@
 // takes ~3 us to land under load, so an SM needs ~130 KB in flight to draw its share of the bandwidth.
 // Separate kernels per matvec cannot keep that: each boundary drains the pipeline, and co-residency
 // with the next kernel caps the ring at half the shared memory.  Here one producer warp per CTA walks
-// the weight stages of ALL phases in order through a ring of 22 (or 11) slots in ~215 KB of shared
+// the weight stages of ALL phases in order through a ring of 33 (or 22, 11) slots in ~215 KB of shared
 // memory and never waits on a grid barrier: while the consumers sit in a barrier, an activation
 // prologue or the attention phase, the producer is already streaming the next matrices.
 //
 // Consumers: 11 warps, each its own stage group; global stage g goes to warp g % 11 and slot g % nslots
+// (three slots per warp when the largest unit fits a third of the ring: a Llama-7B w2 row, 6.2 KB, does)
 // (nslots is a multiple of 11, so a slot always serves one warp and the parity waits stay one phase
 // apart).  A warp works alone on the units (rows, or the RoPE / SwiGLU row pairs) of its stages: lane l
 // takes blocks l, l+32, ... of the row (the first four held in registers as Q8_0 activations for the
@@ -988,7 +989,7 @@ bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t s
     const int64_t tree = r128((int64_t)(NCW / 2) * GMAX * (hd + 2) * 4);  // [warps handing over][GMAX][hd + 2]
     (void)group;
     const int64_t scratch = std::max(act, tree);
-    for (int ns : {2 * NG, NG}) {  // slots: a multiple of NG, so every slot belongs to one group
+    for (int ns : {3 * NG, 2 * NG, NG}) {  // slots: a multiple of NG, so every slot belongs to one group
         const int64_t bars = r128((int64_t)ns * 2 * 8);  // full[ns], empty[ns]
         const int64_t avail = (int64_t)smem_optin - (bars + scratch + kRedBytes);
         const int64_t slot = (avail / ns) / 128 * 128;
