@@ -49,6 +49,12 @@ int qmc_stream(void **stream);
 int qmc_sync(void);
 /* reads and clears the device error word set by bounded waits; returns QMC_ETIMEOUT if it was set */
 int qmc_check_device_error(void);
+/* failure-detection self-test: runs ONE device-side bounded wait that nothing satisfies and returns once
+ * the kernel has given up (after the wait limit, ~2 s).  kind 0: the grid-barrier counter poll of the
+ * decode step; kind 1: an mbarrier wait of the weight pipeline, after one real bulk copy has landed.
+ * The error word is left set, so the next qmc_check_device_error() returns QMC_ETIMEOUT (and clears it);
+ * no fault is raised and the context stays usable.  *ms (may be NULL) receives the kernel's duration. */
+int qmc_wait_selftest(int kind, float *ms);
 
 /* ---- device buffers (for host layers that own no CUDA code) ---- */
 /* page-lock [ptr, ptr + bytes) of host memory (read-only mappings allowed, e.g. a mapped .qlm) so that

@@ -71,6 +71,7 @@ _CUDA_SIGS = {
     "qmc_stream": (I, [C.POINTER(V)]),
     "qmc_sync": (I, []),
     "qmc_check_device_error": (I, []),
+    "qmc_wait_selftest": (I, [I, C.POINTER(F)]),
     "qmc_malloc": (I, [C.POINTER(V), S]),
     "qmc_free": (I, [V]),
     "qmc_memcpy_h2d": (I, [V, V, S, V]),

@@ -102,6 +102,31 @@ using namespace qmc;
     if (!c_) return QMC_ECUDA;                                                                                         \
     (void)c_
 
+namespace qmc {
+// One bounded wait that nothing satisfies, written with the helpers the decode and matvec kernels wait
+// with: kind 0 polls a grid-barrier counter no CTA raises; kind 1 lands one real bulk copy on an
+// mbarrier (phase 0) and then waits for a phase 1 that no copy completes.  The kernel gives up after the
+// wait limit, ORs its code into the error word and returns; nothing faults and the context stays usable.
+__global__ void wait_selftest_kernel(int kind, const unsigned *ctr, const uint8_t *src, int *err) {
+    __shared__ __align__(128) uint8_t buf[256];
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    if (kind == 0) {
+        if (!counter_wait(ctr, 1u)) raise_error(err, kErrFlagTimeout);
+        return;
+    }
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_arrive_tx(&bar, sizeof buf);
+    bulk_g2s(buf, src, sizeof buf, &bar);
+    if (!mbar_wait(&bar, 0)) {  // the copy itself did not land
+        raise_error(err, kErrMbarTimeout);
+        return;
+    }
+    if (!mbar_wait(&bar, 1)) raise_error(err, kErrMbarTimeout);
+}
+}  // namespace qmc
+
 extern "C" {
 
 const char *qmc_last_error(void) { return g_err; }
@@ -145,6 +170,33 @@ int qmc_check_device_error(void) {
         return set_error(QMC_ETIMEOUT, "a device-side bounded wait expired (code %d)", v);
     }
     return QMC_OK;
+}
+
+int qmc_wait_selftest(int kind, float *ms) {
+    CTX_OR_FAIL();
+    if (kind != 0 && kind != 1) return set_error(QMC_EINVAL, "wait_selftest: kind %d is not 0 or 1", kind);
+    uint8_t *buf = nullptr;  // [0, 4): the counter (0); [256, 512): the copy's source
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    int rc = QMC_OK;
+    cudaError_t e = cudaMalloc(&buf, 512);
+    if (e == cudaSuccess) e = cudaMemsetAsync(buf, 0, 512, c_->stream);
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, c_->stream);
+    if (e == cudaSuccess) {
+        wait_selftest_kernel<<<1, 32, 0, c_->stream>>>(kind, (const unsigned *)buf, buf + 256, c_->err);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(e1, c_->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c_->stream);
+    float t = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
+    if (e != cudaSuccess) rc = cuda_fail(e, "wait_selftest");
+    else if (ms) *ms = t;
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (buf) cudaFree(buf);
+    return rc;
 }
 
 int qmc_host_register(const void *ptr, size_t bytes) {

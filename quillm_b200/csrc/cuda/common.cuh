@@ -129,6 +129,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         if (clock64() - t0 > kWaitCycles) return false;
     return true;
 }
+// bounded wait against a deadline several waits share (t0 + kWaitCycles)
+__device__ __forceinline__ bool mbar_wait_since(uint64_t *bar, uint32_t parity, long long t0) {
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// bounded poll of a counter other CTAs raise: true once *ctr reached `target` (modulo 2^32), false after
+// ~kWaitCycles
+__device__ __forceinline__ bool counter_wait(const unsigned *ctr, unsigned target) {
+    const long long t0 = clock64();
+    while ((int)(ld_acquire(ctr) - target) < 0)
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
 // global -> shared bulk copy completing on `bar`; dst, src 16-byte aligned, bytes % 16 == 0
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

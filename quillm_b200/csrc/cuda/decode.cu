@@ -123,16 +123,8 @@ __device__ __forceinline__ unsigned long long *trace_stage(const DecodeParams &p
 #define DTRACE_ADD(ph, k, v) do { if (unsigned long long *q_ = trace_slot(ph, k)) atomicAdd(q_, (unsigned long long)(v)); } while (0)
 #define DTRACE_MAX(ph, k, v) do { if (unsigned long long *q_ = trace_slot(ph, k)) atomicMax(q_, (unsigned long long)(v)); } while (0)
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
 }
 __device__ __forceinline__ void split_units(int64_t units, int64_t &u0, int64_t &u1) {
     u0 = (int64_t)blockIdx.x * units / gridDim.x;
@@ -159,14 +151,9 @@ __device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, b
         int ok = 1;
         DTRACE_SET((int)(target / gridDim.x) - 1, kTrArrive, gtime());
         red_release_add(p.gbar, 1u);
-        if (!dead) {
-            const long long t0 = clock64();
-            while ((int)(ld_acquire(p.gbar) - target) < 0)
-                if (clock64() - t0 > kWaitCycles) {
-                    raise_error(p.err, kErrFlagTimeout);
-                    ok = 0;
-                    break;
-                }
+        if (!dead && !counter_wait(p.gbar, target)) {
+            raise_error(p.err, kErrFlagTimeout);
+            ok = 0;
         }
         *flag = ok;
     }
@@ -216,6 +203,7 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
         }
     };
     settle();
+    unsigned g_last = 0, nissued = 0;  // this lane's last issued stage and its count (for the drain)
     const long long t0 = clock64();
     while (true) {
         bool done = i >= p.nph, issued = false;
@@ -231,19 +219,34 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
                 if (unsigned long long *q_ = trace_stage(p, g, 0)) *q_ = gtime();
                 mbar_arrive_tx(&full[s], bytes);
                 bulk_g2s(sm + (size_t)s * p.slot_bytes, q.W + ua * ubytes, bytes, &full[s]);
+                g_last = g, nissued++;
                 k += NG;
                 settle();
                 issued = true;
             }
         }
         constexpr unsigned kLanes = (1u << NG) - 1u;  // lanes 0..NG-1 run this loop together
-        if (!__any_sync(kLanes, !done)) return;
+        if (!__any_sync(kLanes, !done)) break;
         if (!__any_sync(kLanes, issued)) {  // every lane waits on a slot: back off briefly
             __nanosleep(64);
             if (__any_sync(kLanes, clock64() - t0 > kWaitCycles)) {  // warp-uniform: all lanes leave together
                 if (!done) raise_error(p.err, kErrMbarTimeout);
-                return;
+                break;
             }
+        }
+    }
+    // drain: the CTA must not exit while a copy into its shared memory is in flight.  A slot is refilled
+    // only after its consumer saw the previous copy land, so the copies that can still be in flight are
+    // this lane's last one per slot (stages g_last, g_last - NG, ...); after a timeout nobody consumes
+    // them, so wait for them here (bounded; in a normal step they landed long ago or land for the
+    // consumers anyway)
+    const long long td = clock64();
+    const unsigned per_lane = (unsigned)(p.nslots / NG);
+    for (unsigned j = 0; j < nissued && j < per_lane; j++) {
+        const unsigned g = g_last - j * NG;
+        if (!mbar_wait_since(&full[g % (unsigned)p.nslots], (g / p.nslots) & 1u, td)) {
+            raise_error(p.err, kErrMbarTimeout);
+            break;
         }
     }
 }
@@ -721,7 +724,9 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         if (lane == 0)
             if (unsigned long long *q_ = trace_stage(p, g, 3))
                 *q_ = gtime() | (mbar_test(&full[s], (g / p.nslots) & 1u) ? (1ull << 63) : 0ull);
-        if (!dead && !mbar_wait(&full[s], (g / p.nslots) & 1u)) {
+        // warp-uniform verdict: a lane that timed out while another saw the copy land makes the whole warp
+        // dead, so no lane computes on a stage that may still be filling and the shuffles stay full-warp
+        if (!dead && __any_sync(0xffffffffu, !mbar_wait(&full[s], (g / p.nslots) & 1u))) {
             dead = true;
             if (lane == 0) raise_error(p.err, kErrMbarTimeout);
         }
@@ -745,7 +750,8 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         __syncwarp();
         if (lane == 0)
             if (unsigned long long *q_ = trace_stage(p, g, 2)) *q_ = gtime_after(pa0 + pa1);
-        if (lane == 0) mbar_arrive(&empty[s]);
+        // a dead warp releases nothing: its slot may still be filling, and the producer must not refill it
+        if (lane == 0 && !dead) mbar_arrive(&empty[s]);
     }
     if (!dead) flush();
     gk += (unsigned)nst;

@@ -109,9 +109,6 @@ __device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int
         if (cp[i].tma) bulk_g2s(dst[i], src[i] + cp[i].a0, cp[i].tma, bar);
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -325,7 +322,8 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
 
     if (warp == NCW) {  // producer: refill each stage once its consumers released it
         if (lane == 0) {
-            for (int k = p.nstages; k < nst; k++) {
+            int k = min(p.nstages, nst);  // stages issued so far
+            for (; k < nst; k++) {
                 const int s = k % p.nstages;
                 if (!mbar_wait(&empty[s], (uint32_t)((k / p.nstages) - 1) & 1u)) {
                     raise_error(p.err, kErrMbarTimeout);
@@ -333,6 +331,14 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
                 }
                 issue_stage(p, sm + (int64_t)s * p.stage_bytes, &full[s], u0, u1, k);
             }
+            // drain: the last copy of each slot may still be in flight; consumers that timed out will not
+            // wait for it, and the CTA must not exit before it lands (bounded)
+            const long long td = clock64();
+            for (int j = max(0, k - p.nstages); j < k; j++)
+                if (!mbar_wait_since(&full[j % p.nstages], (uint32_t)(j / p.nstages) & 1u, td)) {
+                    raise_error(p.err, kErrMbarTimeout);
+                    break;
+                }
         }
         return;
     }
@@ -346,11 +352,15 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
     const int grp = warp / GW, wig = warp % GW;
     const int g = p.g, sub = wig % g, bstep = 32 * g;
     unsigned long long best = 0;
+    // After a timeout a warp keeps running the loop (on stale stage data) so that every named barrier it
+    // shares with other warps is still met, but waits for no more copies and releases no more slots:
+    // the producer then never refills a slot whose copy may still be in flight.
+    bool dead = false;
     for (int k = grp; k < nst; k += NG) {  // this group's stages
         const int s = k % p.nstages;
-        if (!mbar_wait(&full[s], (uint32_t)(k / p.nstages) & 1u)) {
+        if (!dead && __any_sync(0xffffffffu, !mbar_wait(&full[s], (uint32_t)(k / p.nstages) & 1u))) {
+            dead = true;
             if (lane == 0) raise_error(p.err, kErrMbarTimeout);
-            return;
         }
         const int64_t ua = u0 + (int64_t)k * p.R;
         const int n = (int)min((int64_t)p.R, u1 - ua);
@@ -393,7 +403,7 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0 && !dead) mbar_arrive(&empty[s]);
     }
     if (p.epi == EPI_LOGITS) logits_argmax(p, sm, best, warp, lane);
 }
