@@ -50,6 +50,10 @@ float *qm_model_prefill(qm_model *m, const int32_t *tokens, int32_t n, int32_t p
 /* greedy generation kept on the device (prompt fed one token per step, then n_gen argmax tokens);
  * 0 on success */
 int qm_model_generate(qm_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen, int32_t *out_tokens);
+/* KV cache element type after load and before the first step: 0 = fp32 (the reference's cache, the
+ * default), 1 = fp16 (half the cache bytes and attention reads; its own tolerance).  0 on success, -1
+ * otherwise (bad dtype, or the model has already run a step). */
+int qm_model_set_kv_dtype(qm_model *m, int dtype);
 
 #pragma GCC visibility pop
 #endif

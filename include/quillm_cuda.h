@@ -37,7 +37,7 @@ enum {
 };
 
 /* tensor dtypes: the .qlm / qm_dtype values (src/qm_base.h:11-15) */
-enum { QMC_F32 = 0, QMC_Q8_0 = 2, QMC_Q4_0 = 3 };
+enum { QMC_F32 = 0, QMC_F16 = 1 /* KV cache only */, QMC_Q8_0 = 2, QMC_Q4_0 = 3 };
 
 const char *qmc_last_error(void);
 int qmc_device_count(int *count);
@@ -101,6 +101,18 @@ int qmc_matmul_nt_q(int dtype, const void *W, const float *A, float *C, int64_t 
  * default stream. */
 int qmc_matmul_nt_q_noalloc(int dtype, const void *W, const float *A, float *C, int64_t T, int64_t N, int64_t K,
                             void *stream);
+
+/* Split-row weight layout: each row is its ceil(K/32) fp16 block scales (padded to a 16-byte multiple)
+ * followed by the blocks' quant bytes (32 per Q8_0 block, 16 per Q4_0 block), so every payload is
+ * 16-byte aligned; same numbers as the file's blocks, regrouped.  qmc_split_row_bytes gives the row
+ * size; qmc_repack_split writes rows x that many bytes to dst from a .qlm-layout (AoS) matrix. */
+int64_t qmc_split_row_bytes(int dtype, int64_t K);
+int qmc_repack_split(int dtype, const void *W, int64_t rows, int64_t K, void *dst, void *stream);
+/* qmc_matmul_nt_q on the tensor cores (tcgen05.mma kind::i8: one MMA per 32-element block gives the
+ * exact int32 block dots, the epilogue applies the block scales in the reference's order), for a
+ * split-row weight: the same C bit for bit.  The model's batched prompt forward uses it. */
+int qmc_matmul_split_q(int dtype, const void *Wsplit, const float *A, float *C, int64_t T, int64_t N, int64_t K,
+                       void *stream);
 
 /* ---- elementwise, in place on device buffers (src/ops.c:93-133) ---- */
 int qmc_rmsnorm(float *out, const float *x, const float *w, int64_t n, float eps, void *stream);
@@ -168,6 +180,12 @@ int qmc_model_step_bytes(const qmc_model *m, int32_t pos, double *bytes);
  * single-launch persistent path: one GPU, Q8_0/Q4_0 matrices; otherwise one per operation), *persistent =
  * 1 for that path.  Before the first step both are 0. */
 int qmc_model_decode_info(const qmc_model *m, int32_t *launches, int32_t *persistent);
+/* element type of the KV cache: QMC_F32 (default; the reference's fp32 cache, src/model.c:96) or
+ * QMC_F16 (each K after RoPE and each V rounded to nearest-even fp16 when stored: half the cache bytes
+ * and half the attention reads, numerics beyond the reference's contract).  Only before the model's
+ * first step (QMC_ESTATE after it); the cache is reallocated and zeroed. */
+int qmc_model_set_kv_dtype(qmc_model *m, int dtype);
+int qmc_model_kv_dtype(const qmc_model *m, int *dtype);
 int qmc_model_free(qmc_model *m);
 
 /* ---- device-side sampler: temperature / top-k / top-p with the reference's xorshift64* stream

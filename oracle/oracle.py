@@ -49,6 +49,7 @@ def orc():
             "orc_argmax": (I32, [V, I32]),
             "orc_model_open": (V, [C.c_char_p, I, C.c_char_p, S]), "orc_model_close": (None, [V]),
             "orc_model_config": (None, [V, V, V]), "orc_model_forward": (C.POINTER(F), [V, I32, I32]),
+            "orc_model_set_kv_f16": (None, [V, I]),
             "orc_synth_normal": (D, [C.c_uint64, C.c_uint64, C.c_uint64]),
             "orc_synth_rows": (None, [C.c_uint64, C.c_uint64, I64, I64, I64, D, V]),
             "orc_synth_write": (I, [C.c_char_p, V, F, F, I, C.c_uint64, D, I]),
@@ -178,11 +179,13 @@ def synth_write(path: str, cfg: dict, dtype: int, seed: int, std: float, threads
 class OracleModel:
     """the restated forward (qm_oracle.c) on a .qlm file"""
 
-    def __init__(self, path: str, max_seq: int = 0):
+    def __init__(self, path: str, max_seq: int = 0, kv_f16: bool = False):
         err = C.create_string_buffer(256)
         self.h = orc().orc_model_open(path.encode(), max_seq, err, 256)
         if not self.h:
             raise RuntimeError(err.value.decode())
+        if kv_f16:
+            orc().orc_model_set_kv_f16(self.h, 1)
         cfg = (C.c_int32 * 7)()
         fc = (C.c_float * 2)()
         orc().orc_model_config(self.h, cfg, fc)

@@ -319,6 +319,7 @@ struct orc_model {
     const orc_tensor **lay; /* [L][9]: attn_norm wq wk wv wo ffn_norm w1 w2 w3 */
     float *x, *xb, *xb2, *q, *hb, *hb2, *att, *logits, *kc, *vc;
     uint8_t *xq;
+    int kv_f16;
 };
 
 static uint32_t rd32(const uint8_t *p) { return (uint32_t)p[0] | (uint32_t)p[1] << 8 | (uint32_t)p[2] << 16 | (uint32_t)p[3] << 24; }
@@ -445,6 +446,8 @@ void orc_model_close(orc_model *m) {
     free(m);
 }
 
+void orc_model_set_kv_f16(orc_model *m, int on) { m->kv_f16 = on != 0; }
+
 void orc_model_config(const orc_model *m, int32_t cfg[7], float fcfg[2]) {
     memcpy(cfg, m->cfg, sizeof m->cfg);
     fcfg[0] = m->theta;
@@ -471,6 +474,11 @@ const float *orc_model_forward(orc_model *m, int32_t token, int32_t pos) {
         mv(m, L[3], m->xb, vslot);
         orc_rope(m->q, c[3], hd, pos, m->theta);
         orc_rope(kslot, c[4], hd, pos, m->theta);
+        if (m->kv_f16)
+            for (int64_t i = 0; i < KV; i++) {
+                kslot[i] = orc_fp16_to_fp32(orc_fp32_to_fp16(kslot[i]));
+                vslot[i] = orc_fp16_to_fp32(orc_fp32_to_fp16(vslot[i]));
+            }
         const float *kl = m->kc + (size_t)l * S * KV, *vl = m->vc + (size_t)l * S * KV;
         for (int64_t h = 0; h < c[3]; h++) {
             int64_t g = h / grp;

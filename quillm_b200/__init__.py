@@ -17,7 +17,7 @@ LIBDIR = os.path.join(HERE, "lib")
 CUDA_LIB = os.path.join(LIBDIR, "libquillm_cuda.so")
 HOST_LIB = os.path.join(LIBDIR, "libquillm.so")
 
-QMC_F32, QMC_Q8_0, QMC_Q4_0 = 0, 2, 3
+QMC_F32, QMC_F16, QMC_Q8_0, QMC_Q4_0 = 0, 1, 2, 3  # QMC_F16: KV cache only
 (QMC_T_TOK_EMBD, QMC_T_NORM, QMC_T_OUTPUT, QMC_T_ATTN_NORM, QMC_T_WQ, QMC_T_WK, QMC_T_WV, QMC_T_WO,
  QMC_T_FFN_NORM, QMC_T_W1, QMC_T_W2, QMC_T_W3) = range(12)
 STATUS = {0: "ok", -1: "invalid argument", -2: "cuda error", -3: "out of memory", -4: "nccl error",
@@ -71,6 +71,9 @@ _CUDA_SIGS = {
     "qmc_stream": (I, [C.POINTER(V)]),
     "qmc_sync": (I, []),
     "qmc_check_device_error": (I, []),
+    "qmc_split_row_bytes": (I64, [I, I64]),
+    "qmc_repack_split": (I, [I, P, I64, I64, P, V]),
+    "qmc_matmul_split_q": (I, [I, P, P, P, I64, I64, I64, V]),
     "qmc_wait_selftest": (I, [I, C.POINTER(F)]),
     "qmc_malloc": (I, [C.POINTER(V), S]),
     "qmc_free": (I, [V]),
@@ -104,6 +107,8 @@ _CUDA_SIGS = {
     "qmc_model_config": (I, [V, C.POINTER(QmcConfig)]),
     "qmc_model_step_bytes": (I, [V, I32, C.POINTER(D)]),
     "qmc_model_decode_info": (I, [V, C.POINTER(I32), C.POINTER(I32)]),
+    "qmc_model_set_kv_dtype": (I, [V, I]),
+    "qmc_model_kv_dtype": (I, [V, C.POINTER(I)]),
     "qmc_model_free": (I, [V]),
     "qmc_sampler_create": (I, [I32, F, I32, F, C.c_uint64, P]),
     "qmc_sampler_enqueue": (I, [V, P, P, V]),
@@ -153,6 +158,7 @@ _HOST_SIGS = {
     "qm_model_forward": (C.POINTER(C.c_float), [C.POINTER(QmModel), I32, I32]),
     "qm_model_generate": (I, [C.POINTER(QmModel), P, I32, I32, P]),
     "qm_model_prefill": (C.POINTER(C.c_float), [C.POINTER(QmModel), P, I32, I32]),
+    "qm_model_set_kv_dtype": (I, [C.POINTER(QmModel), I]),
 }
 
 
@@ -232,7 +238,8 @@ class Sampler:
 class Model:
     """A libquillm_cuda model (qmc_model*) on the current device."""
 
-    def __init__(self, cfg: dict, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None):
+    def __init__(self, cfg: dict, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
+                 kv_dtype: int = QMC_F32):
         self.lib = cuda()
         self.cfg = QmcConfig(cfg["dim"], cfg["hidden_dim"], cfg["n_layers"], cfg["n_heads"], cfg["n_kv_heads"],
                              cfg["vocab_size"], cfg["max_seq"], cfg.get("rope_theta", 10000.0),
@@ -240,6 +247,17 @@ class Model:
         self.h = C.c_void_p()
         idbuf = C.create_string_buffer(nccl_id, 128) if nccl_id else None
         check(self.lib.qmc_model_create(C.byref(self.cfg), tp_rank, tp_size, idbuf, C.byref(self.h)), "model_create")
+        if kv_dtype != QMC_F32:
+            self.set_kv_dtype(kv_dtype)
+
+    def set_kv_dtype(self, dtype: int) -> None:
+        """KV cache element type, QMC_F32 (default) or QMC_F16; before the first step only"""
+        check(self.lib.qmc_model_set_kv_dtype(self.h, dtype), "set_kv_dtype")
+
+    def kv_dtype(self) -> int:
+        d = C.c_int(0)
+        check(self.lib.qmc_model_kv_dtype(self.h, C.byref(d)), "kv_dtype")
+        return d.value
 
     def synthesize(self, dtype: int, seed: int, std: float) -> None:
         check(self.lib.qmc_model_synthesize(self.h, dtype, seed, std), "model_synthesize")

@@ -1,4 +1,5 @@
-// Decode attention over the device-resident fp32 KV cache (src/model.c:132-156), split over positions.
+// Decode attention over the device-resident KV cache (fp32 as src/model.c:132-156, or fp16), split over
+// positions.
 //
 // Batch-1 decode has only n_kv_heads (x group) heads, far fewer than the 148 SMs, so each KV head's
 // positions 0..pos are split into `nsplit` chunks, one CTA each, and the nsplit CTAs of a head form one
@@ -21,14 +22,15 @@ constexpr int AT = 128;  // threads per CTA (4 warps)
 constexpr int GMAX = 8;  // query heads per CTA (a larger GQA group spans several CTAs)
 
 struct AParams {
-    const float *q, *kc, *vc;
+    const float *q;
+    const void *kc, *vc;  // float or __half elements
     float *out;
     const int *pos;
     int hd, group, gsplit, kvl, nsplit;
     float scale;
 };
 
-template <int MAXW>
+template <int MAXW, typename KT>
 __global__ void __launch_bounds__(AT) attn_decode_kernel(const AParams p) {
     extern __shared__ __align__(16) float sm[];
     cg::cluster_group cluster = cg::this_cluster();
@@ -43,7 +45,7 @@ __global__ void __launch_bounds__(AT) attn_decode_kernel(const AParams p) {
     const int chunk = (npos + p.nsplit - 1) / p.nsplit;
     const int t0 = split * chunk, t1 = min(npos, t0 + chunk);
     const int64_t hq = (int64_t)kvh * p.group + h0;  // first query head of this CTA
-    const float *kb = p.kc + (int64_t)kvh * hd, *vb = p.vc + (int64_t)kvh * hd;
+    const KT *kb = (const KT *)p.kc + (int64_t)kvh * hd, *vb = (const KT *)p.vc + (int64_t)kvh * hd;
 
     float q[GMAX][MAXW], o[GMAX][MAXW], m[GMAX], l[GMAX];
 #pragma unroll
@@ -62,8 +64,8 @@ __global__ void __launch_bounds__(AT) attn_decode_kernel(const AParams p) {
 #pragma unroll
         for (int w = 0; w < MAXW; w++) {
             const int d = lane + 32 * w;
-            k[w] = d < hd ? kb[(int64_t)tt * p.kvl + d] : 0.0f;
-            v[w] = d < hd ? vb[(int64_t)tt * p.kvl + d] : 0.0f;
+            k[w] = d < hd ? kv_ld(kb + (int64_t)tt * p.kvl + d) : 0.0f;
+            v[w] = d < hd ? kv_ld(vb + (int64_t)tt * p.kvl + d) : 0.0f;
         }
 #pragma unroll
         for (int g = 0; g < GMAX; g++) {
@@ -127,9 +129,9 @@ __global__ void __launch_bounds__(AT) attn_decode_kernel(const AParams p) {
     cluster.sync();  // rank 0 has finished reading the other CTAs' shared memory
 }
 
-template <int MAXW>
+template <int MAXW, typename KT>
 int launch_t(const AttnPlan &a, const AParams &p, int n_kv_local, cudaStream_t s, bool pdl) {
-    auto fn = attn_decode_kernel<MAXW>;
+    auto fn = attn_decode_kernel<MAXW, KT>;
     QMC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     cudaLaunchConfig_t c = {};
     cudaLaunchAttribute attr[2];
@@ -165,16 +167,22 @@ AttnPlan plan_attention(int n_kv_local, int group, int hd, int max_seq, int num_
     return a;
 }
 
-int launch_attention(const AttnPlan &a, const float *q, const float *kc, const float *vc, float *out, float *part,
-                     int *cnt, const int *pos, int n_kv_local, int group, int hd, int kvl, cudaStream_t s, bool pdl) {
+template <typename KT>
+int launch_kt(const AttnPlan &a, const AParams &p, int n_kv_local, int hd, cudaStream_t s, bool pdl) {
+    if (hd <= 32) return launch_t<1, KT>(a, p, n_kv_local, s, pdl);
+    if (hd <= 64) return launch_t<2, KT>(a, p, n_kv_local, s, pdl);
+    if (hd <= 128) return launch_t<4, KT>(a, p, n_kv_local, s, pdl);
+    return launch_t<8, KT>(a, p, n_kv_local, s, pdl);
+}
+
+int launch_attention(const AttnPlan &a, const float *q, const void *kc, const void *vc, bool kv16, float *out,
+                     float *part, int *cnt, const int *pos, int n_kv_local, int group, int hd, int kvl, cudaStream_t s,
+                     bool pdl) {
     (void)part;
     (void)cnt;
     if (hd > 256 || (hd & 1)) return set_error(QMC_EINVAL, "attention: head_dim %d unsupported", hd);
     AParams p{q, kc, vc, out, pos, hd, group, (group + GMAX - 1) / GMAX, kvl, a.nsplit, 1.0f / sqrtf((float)hd)};
-    if (hd <= 32) return launch_t<1>(a, p, n_kv_local, s, pdl);
-    if (hd <= 64) return launch_t<2>(a, p, n_kv_local, s, pdl);
-    if (hd <= 128) return launch_t<4>(a, p, n_kv_local, s, pdl);
-    return launch_t<8>(a, p, n_kv_local, s, pdl);
+    return kv16 ? launch_kt<__half>(a, p, n_kv_local, hd, s, pdl) : launch_kt<float>(a, p, n_kv_local, hd, s, pdl);
 }
 
 }  // namespace qmc

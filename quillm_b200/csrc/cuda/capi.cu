@@ -10,7 +10,9 @@
 #include "attention.cuh"
 #include "elementwise.cuh"
 #include "gemv.cuh"
+#include "decode.cuh"
 #include "matmul.cuh"
+#include "matmul_tc.cuh"
 
 namespace qmc {
 
@@ -291,6 +293,35 @@ int qmc_matmul_nt_q(int dtype, const void *W, const float *A, float *C, int64_t 
     cudaStream_t s = pick_stream(stream);
     if ((rc = launch_quantize_act(A, T, K, aq, ad, s))) return rc;
     return launch_matmul_q(dtype, W, aq, ad, C, T, N, K, s);
+}
+
+int64_t qmc_split_row_bytes(int dtype, int64_t K) {
+    if ((dtype != QMC_Q8_0 && dtype != QMC_Q4_0) || K <= 0) return 0;
+    return split_row_bytes(dtype, K);
+}
+
+int qmc_repack_split(int dtype, const void *W, int64_t rows, int64_t K, void *dst, void *stream) {
+    CTX_OR_FAIL();
+    if (!W || !dst || K <= 0 || rows < 0) return set_error(QMC_EINVAL, "repack_split: bad arguments");
+    return launch_repack_split(dtype, W, rows, K, dst, split_row_bytes(dtype, K), pick_stream(stream));
+}
+
+int qmc_matmul_split_q(int dtype, const void *Wsplit, const float *A, float *C, int64_t T, int64_t N, int64_t K,
+                       void *stream) {
+    CTX_OR_FAIL();
+    if (T <= 0 || N <= 0) return QMC_OK;
+    if (!Wsplit || !A || !C || K <= 0) return set_error(QMC_EINVAL, "matmul_split_q: bad arguments");
+    if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "matmul_split_q: bad dtype %d", dtype);
+    const int64_t nb = nblocks(K);
+    void *scr = nullptr;
+    const size_t qbytes = (size_t)(T * nb * 32 + 255) / 256 * 256;
+    int rc = ensure_scratch(c_, qbytes + (size_t)T * nb * 4, &scr);
+    if (rc) return rc;
+    int8_t *aq = (int8_t *)scr;
+    float *ad = (float *)((uint8_t *)scr + qbytes);
+    cudaStream_t s = pick_stream(stream);
+    if ((rc = launch_quantize_act(A, T, K, aq, ad, s))) return rc;
+    return launch_matmul_q_tc(dtype, Wsplit, split_row_bytes(dtype, K), aq, ad, C, nullptr, T, N, K, c_->err, s);
 }
 
 }  // extern "C"

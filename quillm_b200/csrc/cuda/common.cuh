@@ -27,6 +27,21 @@ __device__ __forceinline__ uint32_t f2h(float f) {
     return __half_as_ushort(__float2half_rn(f));
 }
 
+// ---------------------------------------------------------------- KV cache elements
+// The cache holds fp32 (the reference's layout, src/model.c:96) or, by choice, fp16: each K (after
+// RoPE) and V value rounded to nearest-even once when stored, widened exactly when read.
+__device__ __forceinline__ float kv_ld(const float *p) { return __ldcg(p); }
+__device__ __forceinline__ float kv_ld(const __half *p) { return __half2float(__ldcg(p)); }
+// stores the pair (a, b) at elements i, i + 1 (i even) of a cache of the given kind
+__device__ __forceinline__ void kv_st2(void *base, bool f16, int64_t i, float a, float b) {
+    if (f16) {
+        __stcg((__half2 *)((__half *)base + i), __floats2half2_rn(a, b));
+    } else {
+        __stcg((float *)base + i, a);
+        __stcg((float *)base + i + 1, b);
+    }
+}
+
 // ---------------------------------------------------------------- warp reductions
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

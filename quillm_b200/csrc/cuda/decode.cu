@@ -36,6 +36,7 @@
 // Every wait is bounded (mbarrier waits, the grid barrier): on expiry a thread raises the error word and
 // continues without waiting, so the launch always ends; the host then reports QMC_ETIMEOUT.
 #include <algorithm>
+#include <type_traits>
 
 #include "decode.cuh"
 
@@ -595,21 +596,34 @@ __device__ __forceinline__ float2 epilogue_operand(const DecodeParams &p, const 
     return make_float2(0.0f, 0.0f);
 }
 
+template <bool KV16>
 __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhase &ph, int64_t unit, float a, float b,
                                          float2 opnd, int pos, unsigned long long &best) {
     switch (ph.kind) {
     case PH_QKV: {  // rows 2u, 2u+1: one RoPE pair of q or k, or two v values
         const int64_t vr = 2 * unit;
         float o0 = a, o1 = b;
-        float *dst;
-        if (vr < p.Dq + p.KVl) {
-            rope_pair(a, b, opnd, o0, o1);
-            dst = vr < p.Dq ? p.q + vr : ph.kc + (int64_t)pos * p.KVl + (vr - p.Dq);
+        if constexpr (!KV16) {  // q, k and v are all fp32: one store pair through a selected pointer
+            float *dst;
+            if (vr < p.Dq + p.KVl) {
+                rope_pair(a, b, opnd, o0, o1);
+                dst = vr < p.Dq ? p.q + vr : (float *)ph.kc + (int64_t)pos * p.KVl + (vr - p.Dq);
+            } else {
+                dst = (float *)ph.vc + (int64_t)pos * p.KVl + (vr - p.Dq - p.KVl);
+            }
+            __stcg(dst, o0);
+            __stcg(dst + 1, o1);
         } else {
-            dst = ph.vc + (int64_t)pos * p.KVl + (vr - p.Dq - p.KVl);
+            if (vr < p.Dq + p.KVl) rope_pair(a, b, opnd, o0, o1);
+            if (vr < p.Dq) {
+                __stcg(p.q + vr, o0);
+                __stcg(p.q + vr + 1, o1);
+            } else if (vr < p.Dq + p.KVl) {
+                kv_st2(ph.kc, true, (int64_t)pos * p.KVl + (vr - p.Dq), o0, o1);
+            } else {
+                kv_st2(ph.vc, true, (int64_t)pos * p.KVl + (vr - p.Dq - p.KVl), o0, o1);
+            }
         }
-        __stcg(dst, o0);
-        __stcg(dst + 1, o1);
         break;
     }
     case PH_WO:
@@ -667,7 +681,7 @@ __device__ __forceinline__ void unit_dot(bool two, const uint8_t *r0, int rbytes
 // row dots and warp sums, and one arrival on each of its group's stages.  Epilogues are deferred: lane
 // k keeps the k-th pending unit's sums, and every 32 units (and at the end of the phase) all lanes run
 // their epilogues at once, their operand loads (RoPE pairs, residual x) in flight together.
-template <int DT>
+template <int DT, bool KV16>
 __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, uint64_t *full, uint64_t *empty,
                            unsigned &gk, bool &dead, int pos, unsigned long long &best, int phi) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, grp = warp / GW, wig = warp % GW;
@@ -711,7 +725,7 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         nunits += npend;
         if (lane < npend) {
             const float2 opnd = first_batch ? opre : epilogue_operand(p, ph, punit, pos);
-            epilogue(p, ph, punit, pa0, pa1, opnd, pos, best);
+            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best);
         }
         npend = 0;
         first_batch = false;
@@ -765,7 +779,18 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
 }
 
 // ---------------------------------------------------------------- attention phase
+// Lane l holds head dimensions dim(w), w < MAXW: fp32 cache, l + 32 w (each K/V element load is one
+// coalesced 128-byte warp access); fp16 cache, the pairs 2 l + 64 i (+1), i < MAXW / 2, read as one
+// half2 each, so a row takes half the load instructions and twice the positions fit the same registers.
+template <bool F16>
+__device__ __forceinline__ int att_dim(int lane, int w) {
+    return F16 ? 64 * (w >> 1) + 2 * lane + (w & 1) : lane + 32 * w;
+}
+
+template <typename KT>  // cache element: float or __half
 __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int pos) {
+    constexpr bool F16 = std::is_same<KT, __half>::value;
+    constexpr int CH = F16 ? 2 * kAttnChunk : kAttnChunk;  // positions per warp loaded together
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int npos = pos + 1, nunit = p.nkv * p.gsplit;
     const int nseg = attn_segments(p, pos);
@@ -775,7 +800,7 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
     const int hd = p.hd, stride = hd + 2, ps = hd + kPartHead;
     const int chunk = (npos + nseg - 1) / nseg, t0 = seg * chunk, t1 = active ? min(npos, t0 + chunk) : 0;
     const int64_t hq = (int64_t)kvh * p.group + h0;  // first query head of this unit
-    const float *kb = ph.kc + (int64_t)kvh * hd, *vb = ph.vc + (int64_t)kvh * hd;
+    const KT *kb = (const KT *)ph.kc + (int64_t)kvh * hd, *vb = (const KT *)ph.vc + (int64_t)kvh * hd;
 
     float q[GMAX][MAXW], o[GMAX][MAXW], m[GMAX], l[GMAX];
 #pragma unroll
@@ -784,41 +809,106 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
         l[g] = 0.0f;
 #pragma unroll
         for (int w = 0; w < MAXW; w++) {
-            const int d = lane + 32 * w;
+            const int d = att_dim<F16>(lane, w);
             q[g][w] = (active && g < G && d < hd) ? __ldcg(p.q + (hq + g) * hd + d) : 0.0f;
             o[g][w] = 0.0f;
         }
     }
-    // positions t0 + warp, + NCW, ...: the K and V rows of up to kAttnChunk of them are loaded at once
-    for (int tb = t0 + warp; tb < t1; tb += kAttnChunk * NCW) {
-        float k[kAttnChunk][MAXW], v[kAttnChunk][MAXW];
+    // positions t0 + warp, + NCW, ...: the K and V rows of up to CH of them are loaded at once
+    for (int tb = t0 + warp; tb < t1; tb += CH * NCW) {
+        float k[CH][MAXW], v[CH][MAXW];
+        if constexpr (F16) {
+            __half2 kh[CH][MAXW / 2], vh[CH][MAXW / 2];
 #pragma unroll
-        for (int c = 0; c < kAttnChunk; c++) {
-            const int tt = tb + c * NCW;
+            for (int c = 0; c < CH; c++) {
+                const int tt = tb + c * NCW;
 #pragma unroll
-            for (int w = 0; w < MAXW; w++) {
-                const int d = lane + 32 * w;
-                k[c][w] = (tt < t1 && d < hd) ? __ldcg(kb + (int64_t)tt * p.KVl + d) : 0.0f;
-                v[c][w] = (tt < t1 && d < hd) ? __ldcg(vb + (int64_t)tt * p.KVl + d) : 0.0f;
+                for (int i = 0; i < MAXW / 2; i++) {
+                    const int d = att_dim<true>(lane, 2 * i);  // even, and hd is even: the pair is in range
+                    const bool ok = tt < t1 && d < hd;
+                    kh[c][i] = ok ? __ldcg((const __half2 *)(kb + (int64_t)tt * p.KVl + d)) : __half2();
+                    vh[c][i] = ok ? __ldcg((const __half2 *)(vb + (int64_t)tt * p.KVl + d)) : __half2();
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < CH; c++)
+#pragma unroll
+                for (int i = 0; i < MAXW / 2; i++) {
+                    const float2 kf = __half22float2(kh[c][i]), vf = __half22float2(vh[c][i]);
+                    k[c][2 * i] = kf.x, k[c][2 * i + 1] = kf.y;
+                    v[c][2 * i] = vf.x, v[c][2 * i + 1] = vf.y;
+                }
+        } else {
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                const int tt = tb + c * NCW;
+#pragma unroll
+                for (int w = 0; w < MAXW; w++) {
+                    const int d = att_dim<false>(lane, w);
+                    k[c][w] = (tt < t1 && d < hd) ? kv_ld(kb + (int64_t)tt * p.KVl + d) : 0.0f;
+                    v[c][w] = (tt < t1 && d < hd) ? kv_ld(vb + (int64_t)tt * p.KVl + d) : 0.0f;
+                }
             }
         }
+        if constexpr (!F16) {  // fp32 cache: one online softmax update per position
 #pragma unroll
-        for (int c = 0; c < kAttnChunk; c++) {
-            if (tb + c * NCW >= t1) break;
+            for (int c = 0; c < CH; c++) {
+                if (tb + c * NCW >= t1) break;
 #pragma unroll
-            for (int g = 0; g < GMAX; g++) {
-                if (g < G) {
-                    float sc = 0.0f;
+                for (int g = 0; g < GMAX; g++) {
+                    if (g < G) {
+                        float sc = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < MAXW; w++) sc = fmaf(k[c][w], q[g][w], sc);
-                    sc = warp_sum(sc) * p.scale;
-                    const float mn = fmaxf(m[g], sc);
-                    const float corr = expf(m[g] - mn), e = expf(sc - mn);
-                    l[g] = l[g] * corr + e;
+                        for (int w = 0; w < MAXW; w++) sc = fmaf(k[c][w], q[g][w], sc);
+                        sc = warp_sum(sc) * p.scale;
+                        const float mn = fmaxf(m[g], sc);
+                        const float corr = expf(m[g] - mn), e = expf(sc - mn);
+                        l[g] = l[g] * corr + e;
 #pragma unroll
-                    for (int w = 0; w < MAXW; w++) o[g][w] = o[g][w] * corr + e * v[c][w];
-                    m[g] = mn;
+                        for (int w = 0; w < MAXW; w++) o[g][w] = o[g][w] * corr + e * v[c][w];
+                        m[g] = mn;
+                    }
                 }
+            }
+            continue;
+        }
+        // fp16 cache (twice the positions per chunk): per query head the chunk's scores with their warp
+        // reductions interleaved, then one online softmax update for the whole chunk
+        const int nc = min(CH, (t1 - tb + NCW - 1) / NCW);  // valid positions of this chunk (>= 1)
+#pragma unroll
+        for (int g = 0; g < GMAX; g++) {
+            if (g < G) {
+                float sc[CH];
+#pragma unroll
+                for (int c = 0; c < CH; c++) {
+                    sc[c] = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < MAXW; w++) sc[c] = fmaf(k[c][w], q[g][w], sc[c]);
+                }
+#pragma unroll
+                for (int off = 16; off; off >>= 1)
+#pragma unroll
+                    for (int c = 0; c < CH; c++) sc[c] += __shfl_xor_sync(0xffffffffu, sc[c], off);
+                float mx = m[g];
+#pragma unroll
+                for (int c = 0; c < CH; c++) {
+                    sc[c] *= p.scale;
+                    if (c < nc) mx = fmaxf(mx, sc[c]);
+                }
+                const float corr = expf(m[g] - mx);
+                l[g] *= corr;
+#pragma unroll
+                for (int w = 0; w < MAXW; w++) o[g][w] *= corr;
+#pragma unroll
+                for (int c = 0; c < CH; c++) {
+                    if (c < nc) {
+                        const float e = expf(sc[c] - mx);
+                        l[g] += e;
+#pragma unroll
+                        for (int w = 0; w < MAXW; w++) o[g][w] = fmaf(e, v[c][w], o[g][w]);
+                    }
+                }
+                m[g] = mx;
             }
         }
     }
@@ -833,8 +923,10 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
                     float *dst = scr + ((warp - h) * GMAX + g) * stride;
                     if (lane == 0) dst[0] = m[g], dst[1] = l[g];
 #pragma unroll
-                    for (int w = 0; w < MAXW; w++)
-                        if (lane + 32 * w < hd) dst[2 + lane + 32 * w] = o[g][w];
+                    for (int w = 0; w < MAXW; w++) {
+                        const int d = att_dim<F16>(lane, w);
+                        if (d < hd) dst[2 + d] = o[g][w];
+                    }
                 }
             }
         }
@@ -848,8 +940,10 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
                     const float c1 = l[g] > 0.0f ? expf(m[g] - M) : 0.0f, c2 = l2 > 0.0f ? expf(m2 - M) : 0.0f;
                     l[g] = l[g] * c1 + l2 * c2;
 #pragma unroll
-                    for (int w = 0; w < MAXW; w++)
-                        if (lane + 32 * w < hd) o[g][w] = o[g][w] * c1 + src[2 + lane + 32 * w] * c2;
+                    for (int w = 0; w < MAXW; w++) {
+                        const int d = att_dim<F16>(lane, w);
+                        if (d < hd) o[g][w] = o[g][w] * c1 + src[2 + d] * c2;
+                    }
                     m[g] = M;
                 }
             }
@@ -867,8 +961,10 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
             float *dst = part + g * ps;
             if (lane == 0) __stcg(dst, m[g]), __stcg(dst + 1, l[g]);
 #pragma unroll
-            for (int w = 0; w < MAXW; w++)
-                if (lane + 32 * w < hd) __stcg(dst + kPartHead + lane + 32 * w, o[g][w]);
+            for (int w = 0; w < MAXW; w++) {
+                const int d = att_dim<F16>(lane, w);
+                if (d < hd) __stcg(dst + kPartHead + d, o[g][w]);
+            }
         }
     }
 }
@@ -899,6 +995,7 @@ __device__ void logits_argmax(const DecodeParams &p, uint8_t *sm, unsigned long 
     }
 }
 
+template <bool KV16>  // the KV cache holds fp16 (else fp32): one kernel per cache type
 __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint64_t *full = (uint64_t *)(sm + p.off_bars), *empty = full + p.nslots;
@@ -938,7 +1035,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
         if (t == 0) DTRACE_SET(i, kTrStart, gtime());
         if (i + 1 < p.nph) desc_prefetch(p.ph + i + 1, dsm + ((i + 1) & 1));
         if (ph.kind == PH_ATTN) {
-            attention(p, ph, sm, pos);
+            if constexpr (KV16) attention<__half>(p, ph, sm, pos);
+            else attention<float>(p, ph, sm, pos);
             if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
             continue;
         }
@@ -946,8 +1044,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
         if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
         unsigned long long best = 0;  // this thread's argmax key (OUT phase)
         const bool two = ph.urows == 2;
-        if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
-        else run_matvec<QMC_Q4_0>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
+        if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
+        else run_matvec<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
         if (ph.kind == PH_OUT) logits_argmax(p, sm, best);
     }
 }
@@ -1021,11 +1119,11 @@ bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t s
 int launch_decode(const DecodeParams &p, const DecodePlan &plan, int grid, cudaStream_t s) {
     DevCtx *c = ctx();
     if (!c) return QMC_ECUDA;
-    static bool attr_done[64];
-    if (!attr_done[c->device]) {
-        QMC_CUDA(cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)c->max_smem_optin));
-        attr_done[c->device] = true;
+    auto fn = p.kv16 ? decode_step_kernel<true> : decode_step_kernel<false>;
+    static bool attr_done[64][2];
+    if (!attr_done[c->device][p.kv16 != 0]) {
+        QMC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->max_smem_optin));
+        attr_done[c->device][p.kv16 != 0] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1037,7 +1135,7 @@ int launch_decode(const DecodeParams &p, const DecodePlan &plan, int grid, cudaS
     cfg.blockDim = dim3(NT);
     cfg.dynamicSmemBytes = plan.smem;
     cfg.stream = s;
-    QMC_CUDA(cudaLaunchKernelEx(&cfg, decode_step_kernel, p));
+    QMC_CUDA(cudaLaunchKernelEx(&cfg, fn, p));
     return QMC_OK;
 }
 

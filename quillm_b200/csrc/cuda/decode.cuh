@@ -33,7 +33,7 @@ struct DecodePhase {
     const float *in;      // input vector (x, SwiGLU output; WO merges the attention partials instead)
     const float *norm_w;  // fused rmsnorm weight or null
     float *out;           // WO/W2: x (+=), FFN: h, OUT: logits
-    float *kc, *vc;       // QKV / ATTN: this layer's caches [max_seq][KVl]
+    void *kc, *vc;        // QKV / ATTN: this layer's caches [max_seq][KVl] (float or __half: kv16)
 };
 
 struct DecodeParams {
@@ -57,6 +57,7 @@ struct DecodeParams {
     unsigned *gbar;  // grid barrier arrival counter (zero between steps)
     float *apart;    // attention segment partials [nkv * gsplit][maxseg][4][4 + hd]
     int maxseg;
+    int kv16;  // the KV cache holds fp16 (else fp32)
     int *err;
     int nslots, slot_bytes;
     int off_bars, off_xq, off_xds, off_red;

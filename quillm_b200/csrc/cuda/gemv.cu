@@ -47,7 +47,9 @@ struct KParams {
     const float *x, *norm_w;
     float eps;
     int epi;
-    float *y, *q, *kcache, *vcache;
+    float *y, *q;
+    void *kcache, *vcache;
+    int kv16;
     int Dq, KVl, hd;
     const float2 *rope;
     const int *pos;
@@ -182,15 +184,15 @@ __device__ __forceinline__ void epilogue(const KParams &p, int64_t unit, float a
     } else {  // EPI_QKV: rows 2u, 2u+1 are one RoPE pair inside a head
         const int64_t vr = 2 * unit;
         float o0 = a, o1 = b;
-        float *dst;
-        if (vr < p.Dq + p.KVl) {
-            rope_pair(a, b, p.rope[(int64_t)pos * (p.hd >> 1) + (int)((vr % p.hd) >> 1)], o0, o1);
-            dst = vr < p.Dq ? p.q + vr : p.kcache + (int64_t)pos * p.KVl + (vr - p.Dq);
+        if (vr < p.Dq + p.KVl) rope_pair(a, b, p.rope[(int64_t)pos * (p.hd >> 1) + (int)((vr % p.hd) >> 1)], o0, o1);
+        if (vr < p.Dq) {
+            p.q[vr] = o0;
+            p.q[vr + 1] = o1;
+        } else if (vr < p.Dq + p.KVl) {
+            kv_st2(p.kcache, p.kv16, (int64_t)pos * p.KVl + (vr - p.Dq), o0, o1);
         } else {
-            dst = p.vcache + (int64_t)pos * p.KVl + (vr - p.Dq - p.KVl);
+            kv_st2(p.vcache, p.kv16, (int64_t)pos * p.KVl + (vr - p.Dq - p.KVl), o0, o1);
         }
-        dst[0] = o0;
-        dst[1] = o1;
     }
 }
 
@@ -482,6 +484,7 @@ int launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl, int grid_limit
     p.q = a.q;
     p.kcache = a.kcache;
     p.vcache = a.vcache;
+    p.kv16 = a.kv16;
     p.Dq = a.Dq;
     p.KVl = a.KVl;
     p.hd = a.hd;

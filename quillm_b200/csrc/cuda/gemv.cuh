@@ -24,7 +24,9 @@ struct GemvArgs {
     int epi = EPI_STORE;
     float *y = nullptr;
     // EPI_QKV
-    float *q = nullptr, *kcache = nullptr, *vcache = nullptr;  // caches: layer base, [max_seq][KVl]
+    float *q = nullptr;
+    void *kcache = nullptr, *vcache = nullptr;  // caches: layer base, [max_seq][KVl]
+    int kv16 = 0;                               // caches hold fp16 (else fp32)
     int Dq = 0, KVl = 0, hd = 0;
     const float2 *rope = nullptr;  // [max_seq][hd/2] (cos, sin) rounded to float exactly as src/ops.c:116-118
     const int *pos = nullptr;      // device position

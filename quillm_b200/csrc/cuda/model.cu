@@ -25,6 +25,7 @@
 #include "elementwise.cuh"
 #include "gemv.cuh"
 #include "matmul.cuh"
+#include "matmul_tc.cuh"
 #include "prefill.cuh"
 #include "synth.cuh"
 
@@ -52,7 +53,9 @@ struct qmc_model {
     std::vector<Layer> layers;
     std::vector<void *> allocs;
     float *x = nullptr, *xb = nullptr, *q = nullptr, *h = nullptr, *logits_l = nullptr, *logits = nullptr;
-    float *kc = nullptr, *vc = nullptr, *attn_part = nullptr;
+    void *kc = nullptr, *vc = nullptr;  // [L][max_seq][KVl] of float, or of __half when kv16
+    int kv16 = 0;
+    float *attn_part = nullptr;
     float2 *rope = nullptr;
     int *state = nullptr;  // [0] token  [1] pos  [2] step  [3] prompt length  [8] sampled token
     int *forced = nullptr, *gen = nullptr, *attn_cnt = nullptr;
@@ -85,6 +88,10 @@ struct qmc_model {
 namespace {
 
 int64_t rbytes(int dt, int64_t cols) { return row_bytes(dt, cols); }
+
+// layer l's slice of a KV cache
+size_t kv_layer_bytes(const qmc_model *m) { return (size_t)m->S * m->KVl * (m->kv16 ? 2 : 4); }
+void *kv_layer(const qmc_model *m, void *base, int l) { return (uint8_t *)base + (size_t)l * kv_layer_bytes(m); }
 
 int dalloc(qmc_model *m, void **p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes + 256);  // slack: 16-byte line reads past a tensor's end stay inside
@@ -298,10 +305,9 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
         m->mega = decode_eligible(m, c);
         if (!m->mega) return QMC_OK;
         RC(repack_weights(m));  // allocates the split-row copies the phase list points at
-        const int64_t kvstride = (int64_t)m->S * m->KVl;
         for (int l = 0; l < m->L; l++) {
             Layer &Ly = m->layers[l];
-            float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
+            void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
             DecodePhase qkv = matrix_phase(m, c->num_sms, PH_QKV, Ly.dt[QMC_T_WQ], Ly.sqkv, (m->Dl + 2 * m->KVl) / 2, m->D, 2, m->x,
                                            Ly.attn_norm, nullptr);
             qkv.embed = l == 0;
@@ -349,6 +355,7 @@ int launch_decode_step(qmc_model *m, DevCtx *c) {
     p.amax_ctr = (int *)(m->amax + 1);
     p.gbar = m->gbar;
     p.apart = m->apart, p.maxseg = m->maxseg;
+    p.kv16 = m->kv16;
     p.err = c->err;
     p.nslots = m->plan.nslots, p.slot_bytes = m->plan.slot_bytes;
     p.off_bars = m->plan.off_bars, p.off_xq = m->plan.off_xq, p.off_xds = m->plan.off_xds, p.off_red = m->plan.off_red;
@@ -365,6 +372,16 @@ int step_status(qmc_model *m) {
     return rc;
 }
 
+// per-token calls: the error word comes back with the step's own copies (one synchronisation); only a
+// set word takes the slow path that reads, clears and resets
+int enqueue_err_read(qmc_model *m) {
+    DevCtx *c = ctx();
+    if (!c) return QMC_ECUDA;
+    QMC_CUDA(cudaMemcpyAsync(m->h_state + 15, c->err, 4, cudaMemcpyDeviceToHost, m->stream));
+    return QMC_OK;
+}
+int step_status_read(qmc_model *m) { return m->h_state[15] ? step_status(m) : QMC_OK; }
+
 // enqueue one decode step on m->stream (captured into the graph)
 int enqueue_step(qmc_model *m) {
     cudaStream_t s = m->stream;
@@ -372,10 +389,9 @@ int enqueue_step(qmc_model *m) {
     if (m->mega) return launch_decode_step(m, c);
     const int *pos = m->state + 1;
     RC(launch_embed(m->dt_tok, m->tok, m->D, m->state, m->x, s, true));
-    const int64_t kvstride = (int64_t)m->S * m->KVl;
     for (int l = 0; l < m->L; l++) {
         Layer &Ly = m->layers[l];
-        float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
+        void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
         GemvArgs a;
         a.dtype = Ly.dt[QMC_T_WQ];
         a.W0 = Ly.wqkv;
@@ -388,6 +404,7 @@ int enqueue_step(qmc_model *m) {
         a.q = m->q;
         a.kcache = kcl;
         a.vcache = vcl;
+        a.kv16 = m->kv16;
         a.Dq = m->Dl;
         a.KVl = m->KVl;
         a.hd = m->hd;
@@ -395,7 +412,7 @@ int enqueue_step(qmc_model *m) {
         a.pos = pos;
         a.err = c->err;
         RC(launch_gemv(a, s, true));
-        RC(launch_attention(m->ap, m->q, kcl, vcl, m->xb, m->attn_part, m->attn_cnt, pos, m->NKVl, m->NH / m->NKV,
+        RC(launch_attention(m->ap, m->q, kcl, vcl, m->kv16 != 0, m->xb, m->attn_part, m->attn_cnt, pos, m->NKVl, m->NH / m->NKV,
                             m->hd, m->KVl, s, true));
         GemvArgs o;
         o.dtype = Ly.dt[QMC_T_WO];
@@ -692,8 +709,9 @@ int qmc_model_forward(qmc_model *m, int32_t token, int32_t pos, float *logits_ho
     QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
     if (logits_host) QMC_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, m->stream));
     QMC_CUDA(cudaMemcpyAsync(m->h_state + 4, m->state, 4, cudaMemcpyDeviceToHost, m->stream));
+    RC(enqueue_err_read(m));
     QMC_CUDA(cudaStreamSynchronize(m->stream));
-    RC(step_status(m));
+    RC(step_status_read(m));
     if (logits_host) memcpy(logits_host, m->h_logits, (size_t)m->V * 4);
     if (next_token) *next_token = m->h_state[4];
     return QMC_OK;
@@ -725,6 +743,13 @@ int prefill_proj(qmc_model *m, int dt, const void *W, const float *A, int T, int
     RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream));
     return launch_matmul_q(dt, W, m->pf_aq, m->pf_ad, C, T, N, K, m->stream);
 }
+// the same on the tensor cores, from the split-row copy the decode kernel streams (C2: an interleaved
+// w1/w3 matrix's rows 2i / 2i + 1 go to C / C2)
+int prefill_proj_tc(qmc_model *m, int dt, const uint8_t *Ws, const float *A, int T, int64_t N, int64_t K, float *C,
+                    float *C2) {
+    RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream));
+    return launch_matmul_q_tc(dt, Ws, split_row_bytes(dt, K), m->pf_aq, m->pf_ad, C, C2, T, N, K, ctx()->err, m->stream);
+}
 }  // namespace
 
 int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t pos0, float *logits_host,
@@ -738,26 +763,35 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     RC(prefill_buffers(m, n));
     cudaStream_t s = m->stream;
     DevCtx *c = ctx();
+    if (!complete(m)) return set_error(QMC_ESTATE, "prefill: model incomplete");
+    RC(prepare_decode(m, c));  // quantized single-GPU models: the split-row copies the tensor cores read
+    const bool tc = m->mega;
     const int D = m->D, Dq = m->Dl, KVl = m->KVl, H = m->Hl, NQKV = Dq + 2 * KVl;
     const float eps = m->cfg.norm_eps;
     QMC_CUDA(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
     RC(launch_embed_rows(m->dt_tok, m->tok, D, m->pf_tok, n, m->pf_x, s));
-    const int64_t kvstride = (int64_t)m->S * KVl;
     for (int l = 0; l < m->L; l++) {
         Layer &Ly = m->layers[l];
-        float *kcl = m->kc + l * kvstride, *vcl = m->vc + l * kvstride;
+        void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
         RC(launch_rmsnorm_rows(m->pf_x, Ly.attn_norm, m->pf_xn, n, D, eps, s));
-        RC(prefill_proj(m, Ly.dt[QMC_T_WQ], Ly.wqkv, m->pf_xn, n, NQKV, D, m->pf_qkv));
-        RC(launch_rope_kv_rows(m->pf_qkv, n, Dq, KVl, m->hd, pos0, m->rope, kcl, vcl, s));
+        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WQ], Ly.sqkv, m->pf_xn, n, NQKV, D, m->pf_qkv, nullptr));
+        else RC(prefill_proj(m, Ly.dt[QMC_T_WQ], Ly.wqkv, m->pf_xn, n, NQKV, D, m->pf_qkv));
+        RC(launch_rope_kv_rows(m->pf_qkv, n, Dq, KVl, m->hd, pos0, m->rope, kcl, vcl, m->kv16 != 0, s));
         RC(launch_attn_prefill(m->pf_qkv, n, NQKV, m->NHl, m->NH / m->NKV, m->hd, KVl, pos0, 1.0f / sqrtf((float)m->hd), kcl,
-                               vcl, m->pf_att, s));
-        RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
+                               vcl, m->kv16 != 0, m->pf_att, s));
+        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WO], Ly.swo, m->pf_att, n, D, Dq, m->pf_c, nullptr));
+        else RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
         RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
         RC(launch_rmsnorm_rows(m->pf_x, Ly.ffn_norm, m->pf_xn, n, D, eps, s));
-        RC(prefill_proj(m, Ly.dt[QMC_T_W1], Ly.w1, m->pf_xn, n, H, D, m->pf_h));
-        RC(prefill_proj(m, Ly.dt[QMC_T_W3], Ly.w3, m->pf_xn, n, H, D, m->pf_h3));
+        if (tc) {
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.s13, m->pf_xn, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
+        } else {
+            RC(prefill_proj(m, Ly.dt[QMC_T_W1], Ly.w1, m->pf_xn, n, H, D, m->pf_h));
+            RC(prefill_proj(m, Ly.dt[QMC_T_W3], Ly.w3, m->pf_xn, n, H, D, m->pf_h3));
+        }
         RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
-        RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
+        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_W2], Ly.sw2, m->pf_h, n, D, H, m->pf_c, nullptr));
+        else RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
         RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
     }
     // logits of the last token: the output GEMV with the final rmsnorm fused, as a decode step's
@@ -798,8 +832,9 @@ int qmc_model_forward_sample(qmc_model *m, int32_t token, int32_t pos, qmc_sampl
     QMC_CUDA(cudaGraphLaunch(m->graph, m->stream));
     RC(qmc_sampler_enqueue(s, m->logits, m->state + 8, m->stream));
     QMC_CUDA(cudaMemcpyAsync(m->h_state + 4, m->state + 8, 4, cudaMemcpyDeviceToHost, m->stream));
+    RC(enqueue_err_read(m));
     QMC_CUDA(cudaStreamSynchronize(m->stream));
-    RC(step_status(m));
+    RC(step_status_read(m));
     *next_token = m->h_state[4];
     return QMC_OK;
 }
@@ -868,7 +903,7 @@ int qmc_model_step_bytes(const qmc_model *m, int32_t pos, double *bytes) {
         b += (double)m->D * rbytes(l.dt[QMC_T_WO], m->Dl);
         b += 2.0 * m->Hl * rbytes(l.dt[QMC_T_W1], m->D);
         b += (double)m->D * rbytes(l.dt[QMC_T_W2], m->Hl);
-        b += 2.0 * (pos + 1) * m->KVl * 4.0;  // K and V reads
+        b += 2.0 * (pos + 1) * m->KVl * (m->kv16 ? 2.0 : 4.0);  // K and V reads
     }
     b += (double)m->Vl * rbytes(m->dt_out, m->D);
     *bytes = b;
@@ -884,6 +919,39 @@ int qmc_model_decode_info(const qmc_model *m, int32_t *launches, int32_t *persis
         const bool fused = m->tp == 1 && m->dt_out != QMC_F32;
         *launches = 2 + 5 * m->L + (fused ? 0 : 1);
     }
+    return QMC_OK;
+}
+
+int qmc_model_set_kv_dtype(qmc_model *m, int dtype) {
+    if (!m) return set_error(QMC_EINVAL, "set_kv_dtype: null model");
+    if (dtype != QMC_F32 && dtype != QMC_F16)
+        return set_error(QMC_EINVAL, "set_kv_dtype: dtype %d is not QMC_F32 or QMC_F16", dtype);
+    if (m->graph || m->mega_checked || m->pf_cap)
+        return set_error(QMC_ESTATE, "set_kv_dtype: call it before the model's first step");
+    RC(check_dev(m));
+    if ((dtype == QMC_F16) == (m->kv16 != 0)) return QMC_OK;
+    for (void **buf : {&m->kc, &m->vc}) {  // release the old caches (they hold no positions yet)
+        for (size_t i = 0; i < m->allocs.size(); i++)
+            if (m->allocs[i] == *buf) {
+                m->allocs.erase(m->allocs.begin() + (long)i);
+                break;
+            }
+        QMC_CUDA(cudaFree(*buf));
+        *buf = nullptr;
+    }
+    m->kv16 = dtype == QMC_F16;
+    const size_t bytes = (size_t)m->L * kv_layer_bytes(m);
+    RC(dalloc(m, &m->kc, bytes));
+    RC(dalloc(m, &m->vc, bytes));
+    QMC_CUDA(cudaMemsetAsync(m->kc, 0, bytes, m->stream));
+    QMC_CUDA(cudaMemsetAsync(m->vc, 0, bytes, m->stream));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    return QMC_OK;
+}
+
+int qmc_model_kv_dtype(const qmc_model *m, int *dtype) {
+    if (!m || !dtype) return set_error(QMC_EINVAL, "kv_dtype: null argument");
+    *dtype = m->kv16 ? QMC_F16 : QMC_F32;
     return QMC_OK;
 }
 

@@ -45,7 +45,8 @@ __device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &
 }
 
 __global__ void rope_kv_rows_kernel(float *__restrict__ qkv, int Dq, int KVl, int hd, int pos0,
-                                    const float2 *__restrict__ rope, float *__restrict__ kc, float *__restrict__ vc) {
+                                    const float2 *__restrict__ rope, void *__restrict__ kc, void *__restrict__ vc,
+                                    bool kv16) {
     const int64_t t = blockIdx.x;
     const int pos = pos0 + (int)t;
     float *row = qkv + t * (int64_t)(Dq + 2 * KVl);
@@ -54,24 +55,22 @@ __global__ void rope_kv_rows_kernel(float *__restrict__ qkv, int Dq, int KVl, in
         const int e = 2 * i;  // pair (e, e + 1) of q (e < Dq) or k
         float o0, o1;
         rope_rotate(row[e], row[e + 1], cs[(e % hd) >> 1], o0, o1);
-        if (e < Dq) {
-            row[e] = o0, row[e + 1] = o1;
-        } else {
-            float *dst = kc + (int64_t)pos * KVl + (e - Dq);
-            dst[0] = o0, dst[1] = o1;
-        }
+        if (e < Dq) row[e] = o0, row[e + 1] = o1;
+        else kv_st2(kc, kv16, (int64_t)pos * KVl + (e - Dq), o0, o1);
     }
-    for (int i = threadIdx.x; i < KVl; i += blockDim.x) vc[(int64_t)pos * KVl + i] = row[Dq + KVl + i];
+    for (int i = threadIdx.x; i < KVl >> 1; i += blockDim.x)
+        kv_st2(vc, kv16, (int64_t)pos * KVl + 2 * i, row[Dq + KVl + 2 * i], row[Dq + KVl + 2 * i + 1]);
 }
 
 // one warp per (query head, token): lane l holds q[l + 32 j] (j < 4, head_dim <= 128); the positions are
 // walked 4 at a time with the 4 score reductions interleaved, online softmax (running max, sum, and
 // accumulator rescaled when the max grows)
 constexpr int kPfWarps = 4;  // tokens per block
+template <typename KT>         // cache element: float or __half
 __global__ void __launch_bounds__(32 * kPfWarps) attn_prefill_kernel(const float *__restrict__ qkv, int64_t T, int64_t ldq,
                                                                    int group, int hd, int KVl, int pos0, float scale,
-                                                                   const float *__restrict__ kc,
-                                                                   const float *__restrict__ vc, float *__restrict__ out) {
+                                                                   const KT *__restrict__ kc,
+                                                                   const KT *__restrict__ vc, float *__restrict__ out) {
     const int lane = threadIdx.x & 31;
     const int64_t t = (int64_t)blockIdx.x * kPfWarps + (threadIdx.x >> 5);
     if (t >= T) return;
@@ -84,7 +83,7 @@ __global__ void __launch_bounds__(32 * kPfWarps) attn_prefill_kernel(const float
         q[j] = d < hd ? qkv[t * ldq + (int64_t)h * hd + d] : 0.0f;
         o[j] = 0.0f;
     }
-    const float *kb = kc + (int64_t)kvh * hd, *vb = vc + (int64_t)kvh * hd;
+    const KT *kb = kc + (int64_t)kvh * hd, *vb = vc + (int64_t)kvh * hd;
     float m = -INFINITY, l = 0.0f;
     for (int p0 = 0; p0 < npos; p0 += 4) {
         float sc[4], v[4][4];  // the 4 positions' K and V rows are loaded together
@@ -96,8 +95,8 @@ __global__ void __launch_bounds__(32 * kPfWarps) attn_prefill_kernel(const float
             for (int j = 0; j < 4; j++) {
                 const int d = lane + 32 * j;
                 const bool ok = p < npos && d < hd;
-                if (ok) s = fmaf(q[j], kb[(int64_t)p * KVl + d], s);
-                v[c][j] = ok ? vb[(int64_t)p * KVl + d] : 0.0f;
+                if (ok) s = fmaf(q[j], kv_ld(kb + (int64_t)p * KVl + d), s);
+                v[c][j] = ok ? kv_ld(vb + (int64_t)p * KVl + d) : 0.0f;
             }
             sc[c] = s;
         }
@@ -147,18 +146,23 @@ int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, i
     return QMC_OK;
 }
 
-int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0, const float2 *rope, float *kc,
-                        float *vc, cudaStream_t s) {
-    rope_kv_rows_kernel<<<(unsigned)T, 256, 0, s>>>(qkv, Dq, KVl, hd, pos0, rope, kc, vc);
+int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0, const float2 *rope, void *kc,
+                        void *vc, bool kv16, cudaStream_t s) {
+    rope_kv_rows_kernel<<<(unsigned)T, 256, 0, s>>>(qkv, Dq, KVl, hd, pos0, rope, kc, vc, kv16);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }
 
 int launch_attn_prefill(const float *qkv, int64_t T, int64_t ldq, int n_heads, int group, int hd, int KVl, int pos0,
-                        float scale, const float *kc, const float *vc, float *out, cudaStream_t s) {
+                        float scale, const void *kc, const void *vc, bool kv16, float *out, cudaStream_t s) {
     if (hd > 128) return set_error(QMC_EINVAL, "prefill attention: head_dim %d > 128", hd);
     dim3 grid((unsigned)((T + kPfWarps - 1) / kPfWarps), (unsigned)n_heads);
-    attn_prefill_kernel<<<grid, 32 * kPfWarps, 0, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, kc, vc, out);
+    if (kv16)
+        attn_prefill_kernel<<<grid, 32 * kPfWarps, 0, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const __half *)kc,
+                                                           (const __half *)vc, out);
+    else
+        attn_prefill_kernel<<<grid, 32 * kPfWarps, 0, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const float *)kc,
+                                                           (const float *)vc, out);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }

@@ -11,13 +11,14 @@ int launch_embed_rows(int dtype, const void *table, int64_t cols, const int *tok
 // out[t] = rmsnorm(x[t]) * w, per row as src/ops.c:93-98
 int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, int64_t n, float eps, cudaStream_t s);
 // rows of qkv[T][Dq + 2 KVl] at positions pos0 + t: RoPE on the q pairs (in place) and the k pairs, then
-// k and v stored in the layer's cache slots [pos][KVl] (src/model.c:165-173, src/ops.c:114-126)
-int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0, const float2 *rope, float *kc,
-                        float *vc, cudaStream_t s);
+// k and v stored in the layer's cache slots [pos][KVl] of float, or of __half when kv16
+// (src/model.c:165-173, src/ops.c:114-126)
+int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0, const float2 *rope, void *kc,
+                        void *vc, bool kv16, cudaStream_t s);
 // out[t][h*hd ..] = causal attention of query head h of row t over cache positions 0 .. pos0 + t
 // (src/model.c:132-156), online softmax
 int launch_attn_prefill(const float *qkv, int64_t T, int64_t ldq, int n_heads, int group, int hd, int KVl, int pos0,
-                        float scale, const float *kc, const float *vc, float *out, cudaStream_t s);
+                        float scale, const void *kc, const void *vc, bool kv16, float *out, cudaStream_t s);
 // x += y over n floats (residual, src/model.c:179,186)
 int launch_add(float *x, const float *y, int64_t n, cudaStream_t s);
 

@@ -165,6 +165,14 @@ float *qm_model_prefill(qm_model *m, const int32_t *tokens, int32_t n, int32_t p
     return m->logits;
 }
 
+int qm_model_set_kv_dtype(qm_model *m, int dtype) {
+    if (qmc_model_set_kv_dtype(m->gpu, dtype) != QMC_OK) {
+        qh_fail("qm_model_set_kv_dtype");
+        return -1;
+    }
+    return 0;
+}
+
 int qm_model_generate(qm_model *m, const int32_t *prompt, int32_t n_prompt, int32_t n_gen, int32_t *out_tokens) {
     if (qmc_model_generate(m->gpu, prompt, n_prompt, n_gen, out_tokens) != QMC_OK) {
         qh_fail("qm_model_generate");

@@ -168,6 +168,39 @@ def test_matmul_q_bitwise_equals_scalar_matvec(cuda_dev, dt):
         assert np.array_equal(host(Cd).view(np.uint32), want.view(np.uint32)), (T, N, K)
 
 
+@pytest.mark.parametrize("dt", [O.Q8_0, O.Q4_0])
+def test_matmul_tensor_core_bitwise_equals_scalar_matvec(cuda_dev, dt):
+    """the tcgen05 kind::i8 contraction on split-row weights: bit-identical to the reference's scalar matvec
+    of every row, on ragged T / N / K (partial 128-row and 32-token tiles, a last stage of 1-3 blocks),
+    and with extreme block scales and saturated int8 values"""
+    rng = np.random.default_rng(16)
+    shapes = [(1, 64, 64), (8, 300, 288), (33, 130, 1000), (70, 257, 4096), (128, 1024, 512), (31, 128, 96),
+              (200, 384, 4096), (5, 129, 32)]
+    for T, N, K in shapes:
+        Wf = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        A = rng.standard_normal((T, K)).astype(np.float32)
+        if T == 200:  # outliers: some blocks dominated by one huge value, a zero block, tiny scales
+            Wf[3, :32] = 0.0
+            Wf[5, 7] = 40.0
+            A[1, 100] = 1e4
+            A[2, :32] *= 1e-6
+        W = O.quantize(dt, Wf)
+        want = np.zeros((T, N), np.float32)
+        O.orc().orc_matmul_q(dt, W.ctypes.data, N, K, A.ctypes.data, T, want.ctypes.data)
+        rb = qb.cuda().qmc_split_row_bytes(dt, K)
+        assert rb > 0 and rb % 16 == 0
+        Ws = torch.zeros(N * rb + 256, dtype=torch.uint8, device=cuda_dev)
+        qb.check(qb.cuda().qmc_repack_split(dt, qb.ptr(dev(W, cuda_dev)), N, K, qb.ptr(Ws), None), "repack_split")
+        Cd = torch.full((T, N), float("nan"), dtype=torch.float32, device=cuda_dev)
+        qb.check(qb.cuda().qmc_matmul_split_q(dt, qb.ptr(Ws), qb.ptr(dev(A, cuda_dev)), qb.ptr(Cd), T, N, K, None),
+                 "matmul_split_q")
+        sync()
+        assert qb.cuda().qmc_check_device_error() == 0
+        got = host(Cd)
+        bad = np.argwhere(got.view(np.uint32) != want.view(np.uint32))
+        assert len(bad) == 0, (T, N, K, len(bad), bad[:4].tolist())
+
+
 def test_matmul_f32_within_bound(cuda_dev):
     rng = np.random.default_rng(7)
     for M, N, K in [(4, 4, 8), (1, 150, 600), (40, 150, 600), (37, 65, 1), (128, 96, 333)]:

@@ -151,6 +151,26 @@ def test_oracle_forward_vs_golden_logits(name, tol_deq, tol_fp):
         assert np.array_equal(got.argmax(1), ref.argmax(1))
 
 
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_fp16_cache_option(name):
+    """the oracle's fp16 KV cache (the checker of the device's optional fp16 cache): off, it is the
+    reference's forward bit for bit; on, it moves f32-weight logits by fp16-rounding amounts (more than
+    the fp32 tolerance, under 1e-3 of the float64 truth) with the greedy tokens unchanged, and quantized
+    models stay within 3e-2 of the truth"""
+    toks, V = O.read_tokens(os.path.join(GOLD, f"{name}.tokens"))
+    ref = np.fromfile(os.path.join(GOLD, f"{name}.ref.f32"), np.float32).reshape(len(toks), V)
+    path = os.path.join(GOLD, f"{name}.qlm")
+    a, b = O.OracleModel(path), O.OracleModel(path, kv_f16=True)
+    ga = np.stack([a.forward(t, p) for p, t in enumerate(toks)])
+    gb = np.stack([b.forward(t, p) for p, t in enumerate(toks)])
+    e = np.abs(gb - ref).max() / np.abs(ref).max()
+    if name.endswith("f32"):
+        assert 1e-5 < np.abs(gb - ga).max() / np.abs(ga).max() and e < 1e-3, e
+        assert np.array_equal(gb.argmax(1), ref.argmax(1))
+    else:
+        assert e < 3e-2, e
+
+
 @needs_ref
 @pytest.mark.parametrize("name", [c[0] for c in CASES])
 def test_oracle_forward_bitwise_vs_reference_scalar(name):
