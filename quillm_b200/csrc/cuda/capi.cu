@@ -312,16 +312,16 @@ int qmc_matmul_split_q(int dtype, const void *Wsplit, const float *A, float *C, 
     if (T <= 0 || N <= 0) return QMC_OK;
     if (!Wsplit || !A || !C || K <= 0) return set_error(QMC_EINVAL, "matmul_split_q: bad arguments");
     if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "matmul_split_q: bad dtype %d", dtype);
-    const int64_t nb = nblocks(K);
+    const int64_t nb = nblocks(K), ld = matmul_tc_scale_ld(T);
     void *scr = nullptr;
-    const size_t qbytes = (size_t)(T * nb * 32 + 255) / 256 * 256;
-    int rc = ensure_scratch(c_, qbytes + (size_t)T * nb * 4, &scr);
+    const size_t qbytes = (size_t)(T * nb * 32 + 255) / 256 * 256, dbytes = (size_t)(T * nb * 4 + 255) / 256 * 256;
+    int rc = ensure_scratch(c_, qbytes + dbytes + (size_t)(nb * ld * 4), &scr);
     if (rc) return rc;
     int8_t *aq = (int8_t *)scr;
-    float *ad = (float *)((uint8_t *)scr + qbytes);
+    float *ad = (float *)((uint8_t *)scr + qbytes), *adT = (float *)((uint8_t *)scr + qbytes + dbytes);
     cudaStream_t s = pick_stream(stream);
-    if ((rc = launch_quantize_act(A, T, K, aq, ad, s))) return rc;
-    return launch_matmul_q_tc(dtype, Wsplit, split_row_bytes(dtype, K), aq, ad, C, nullptr, T, N, K, c_->err, s);
+    if ((rc = launch_quantize_act(A, T, K, aq, ad, s, adT, ld))) return rc;
+    return launch_matmul_q_tc(dtype, Wsplit, split_row_bytes(dtype, K), aq, adT, C, nullptr, T, N, K, c_->err, s);
 }
 
 }  // extern "C"

@@ -19,7 +19,7 @@ constexpr int KB = 4;      // quant blocks per K step
 constexpr int WS = KB * 8 + 1;  // padded row stride in 32-bit words
 
 __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t T, int64_t K, int8_t *__restrict__ qs,
-                                    float *__restrict__ d) {
+                                    float *__restrict__ d, float *__restrict__ dT, int64_t ldT) {
     const int lane = threadIdx.x & 31;
     const int64_t nb = nblocks(K);
     const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -30,7 +30,10 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t T, int6
         uint32_t dh;
         const int q = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
         qs[t * nb * 32 + c] = (int8_t)q;
-        if (lane == 0) d[t * nb + b] = dd;
+        if (lane == 0) {
+            d[t * nb + b] = dd;
+            if (dT) dT[b * ldT + t] = dd;
+        }
     }
 }
 
@@ -168,10 +171,11 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float *__restrict__
 
 }  // namespace
 
-int launch_quantize_act(const float *x, int64_t T, int64_t K, int8_t *qs, float *d, cudaStream_t s) {
+int launch_quantize_act(const float *x, int64_t T, int64_t K, int8_t *qs, float *d, cudaStream_t s, float *dT,
+                        int64_t ldT) {
     const int64_t warps = T * nblocks(K);
     const int64_t grid = (warps * 32 + 255) / 256;
-    quantize_act_kernel<<<(int)(grid < 65535 ? grid : 65535), 256, 0, s>>>(x, T, K, qs, d);
+    quantize_act_kernel<<<(int)(grid < 65535 ? grid : 65535), 256, 0, s>>>(x, T, K, qs, d, dT, ldT);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }

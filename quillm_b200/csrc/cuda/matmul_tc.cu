@@ -9,15 +9,25 @@
 // order: the tensor cores do the 32 multiply-adds per (row, token, block), the CUDA cores the 4 float
 // operations.
 //
-// CTA roles (9 warps): warp 0 allocates TMEM and one elected lane issues the MMAs; warps 1-4 are the
-// epilogue (warp w may read TMEM lanes 32 (w % 4) .. + 31, i.e. weight rows of that quarter); warps 5-8
-// produce the shared-memory operands of each stage of KS blocks: the weight blocks (split-row layout:
-// 16-byte aligned payloads) as int8 and the activation blocks, both in the no-swizzle K-major core-matrix
-// layout (a core matrix is 8 rows x 16 bytes; the two 16-byte halves of a block lie 128 bytes apart,
-// 8-row groups 256 bytes apart), plus the blocks' scales.  A ring of NS stages (smem_full / smem_empty)
-// and two TMEM buffers (tmem_full / tmem_empty) keep the three roles overlapped.  Every wait is bounded;
-// after a timeout a role stops, raises the error word and falls through to the end, where the MMA lane
-// first waits (bounded) for the MMAs it issued and warp 0 frees the TMEM it holds.
+// Operands reach shared memory by TMA (cp.async.bulk.tensor, 2-D tiles of 16-byte columns), issued by
+// one producer lane up to NS stages ahead.  A stage holds KS blocks.  Each 16-byte column of a block
+// (half h of block j: Q8_0 weight bytes, activation bytes) lands as a slab [rows][16 bytes], which is
+// the no-swizzle K-major core-matrix layout with 8-row groups 128 bytes apart (SBO) and the two halves
+// of a block one slab apart (LBO).  Q4_0 payloads (16 bytes of nibbles per block) land raw and four
+// converter warps expand them to int8 slabs.  The weight scales (the split row's leading fp16 array) and
+// the block-major activation scales arrive by TMA as well.
+//
+// CTA roles: warp 0 allocates TMEM and one lane issues the MMAs; warps 1-4 are the epilogue (warp w may
+// read TMEM lanes 32 (w % 4) .. + 31, the weight rows of that quarter); warp 5 lane 0 issues the TMA
+// copies; warps 6-9 (Q4_0 only) convert.  Barriers: tma_full (transaction bytes), full (Q4_0: converted),
+// empty (MMA commit + epilogue warps), tmem_full / tmem_empty for two TMEM buffers.  Every wait is
+// bounded; after a timeout a role stops, raises the error word and falls through to the end, where the
+// producer waits (bounded) for its copies in flight, the MMA lane for the MMAs it issued, and warp 0 frees
+// the TMEM it holds.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "matmul_tc.cuh"
 
 namespace qmc {
@@ -27,26 +37,39 @@ constexpr int MT = 128;  // weight rows per CTA (MMA M: TMEM lanes)
 constexpr int NT = 32;   // tokens per CTA (MMA N)
 constexpr int KS = 4;    // blocks per stage
 constexpr int NS = 4;    // stages in the ring
-constexpr int kWarps = 9, kThreads = 32 * kWarps;
 constexpr int kTmemCols = 2 * KS * NT;  // two buffers of KS block tiles (power of 2, >= 32)
 static_assert(kTmemCols == 256, "TMEM allocation size");
 
-// stage layout (bytes)
-constexpr int kWTile = MT * 32, kATile = NT * 32;  // one block's operand tiles
-constexpr int kOffA = KS * kWTile, kOffDw = kOffA + KS * kATile, kOffDa = kOffDw + KS * MT * 4;
-constexpr int kStage = kOffDa + KS * NT * 4;
-constexpr int kOffBars = NS * kStage;  // smem_full[NS], smem_empty[NS], tmem_full[2], tmem_empty[2], tmem addr
-constexpr int kSmem = kOffBars + (2 * NS + 4) * 8 + 16;
-static_assert(kStage % 128 == 0, "stage alignment");
+// stage layout (bytes): int8 weight slabs [2 KS][MT][16], activation slabs [2 KS][NT][16], weight scales
+// [MT][16] (8 blocks' fp16 scales per row; this stage's 4 at byte 8 (g & 1)), activation scales [KS][NT]
+// floats, then (Q4_0) raw nibble slabs [KS][MT][16]
+constexpr int kWSlab = MT * 16, kASlab = NT * 16;
+constexpr int kOffA = 2 * KS * kWSlab, kOffDw = kOffA + 2 * KS * kASlab, kOffDa = kOffDw + MT * 16;
+constexpr int kOffRaw = kOffDa + KS * NT * 4;
+template <int DT>
+__host__ __device__ constexpr int stage_bytes() {
+    return DT == QMC_Q4_0 ? kOffRaw + KS * kWSlab : kOffRaw;
+}
+template <int DT>
+__host__ __device__ constexpr int warps() {
+    return DT == QMC_Q4_0 ? 10 : 6;
+}
+template <int DT>
+__host__ __device__ constexpr int smem_bytes() {
+    return NS * stage_bytes<DT>() + (3 * NS + 4) * 8 + 16;
+}
+static_assert(kOffRaw % 128 == 0 && (kOffRaw + KS * kWSlab) % 128 == 0, "stage alignment");
+// transaction bytes of one stage's TMA copies
+template <int DT>
+__host__ __device__ constexpr uint32_t stage_tx() {
+    return (DT == QMC_Q4_0 ? KS * kWSlab : 2 * KS * kWSlab) + 2 * KS * kASlab + MT * 16 + KS * NT * 4;
+}
 
-// no-swizzle K-major position of byte 16*h of row r inside a block tile
-__device__ __forceinline__ int core_off(int r, int h) { return (r >> 3) * 256 + h * 128 + (r & 7) * 16; }
-
-// shared-memory matrix descriptor: start, leading (K-direction) byte offset 128, stride (8-row group)
-// byte offset 256, descriptor version 1, no swizzle
-__device__ __forceinline__ uint64_t smem_desc(const void *p) {
+// K-major no-swizzle descriptor: start, LBO (between the two 16-byte halves of a block), SBO 128 (between
+// 8-row groups of a slab), descriptor version 1
+__device__ __forceinline__ uint64_t smem_desc(const void *p, uint32_t lbo) {
     const uint64_t a = (smem_u32(p) >> 4) & 0x3fffu;
-    return a | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
+    return a | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
 }
 // instruction descriptor: s32 accumulator, s8 x s8, both K-major, N = NT, M = MT
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(MT >> 4) << 24);
@@ -65,6 +88,15 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
+// 2-D tiled TMA load of box (x, y) of the map into shared memory, completing on bar (no multicast)
+__device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 32 consecutive TMEM columns of this thread's lane
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -80,29 +112,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 struct TcParams {
-    const uint8_t *W;  // split rows: [rows][wstride]: scales (fp16, padded to 16 bytes) then quant payloads
-    int64_t wstride, sbytes;
-    const int8_t *aq;  // activation blocks [T][nb * 32]
-    const float *ad;   // activation scales [T][nb]
-    float *C, *C2;     // C[T][N]; with C2: weight row 2i -> C[t][i], 2i + 1 -> C2[t][i] (N / 2 columns each)
+    int sbytes;     // bytes of a split row's scale array (the payload starts there)
+    float *C, *C2;  // C[T][N]; with C2: weight row 2i -> C[t][i], 2i + 1 -> C2[t][i] (N / 2 columns each)
     int64_t T, N;
     int nb;
     int *err;
 };
 
 template <int DT>
-__global__ void __launch_bounds__(kThreads, 1) matmul_q_tc_kernel(const TcParams p) {
+__global__ void __launch_bounds__(32 * warps<DT>(), 1)
+    matmul_q_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
+                       const __grid_constant__ CUtensorMap smap, const TcParams p) {
+    constexpr int SB = stage_bytes<DT>();
     extern __shared__ __align__(128) uint8_t sm[];
-    uint64_t *full = (uint64_t *)(sm + kOffBars), *empty = full + NS, *tfull = empty + NS, *tempty = tfull + 2;
+    uint64_t *tfull_s = (uint64_t *)(sm + NS * SB), *full = tfull_s + NS, *empty = full + NS, *tfull = empty + NS,
+             *tempty = tfull + 2;
     volatile uint32_t *tmem_slot = (volatile uint32_t *)(tempty + 2);
     volatile int *dead = (volatile int *)(tmem_slot + 1);
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int64_t n0 = (int64_t)blockIdx.x * MT, t0 = (int64_t)blockIdx.y * NT;
+    const int n0 = (int)blockIdx.x * MT, t0 = (int)blockIdx.y * NT;
     const int nst = (p.nb + KS - 1) / KS;
 
     if (t == 0) {
         for (int s = 0; s < NS; s++) {
-            mbar_init(&full[s], 4);       // one arrival per producer warp
+            mbar_init(&tfull_s[s], 1);    // the producer's expect_tx arrival (+ the copies' bytes)
+            mbar_init(&full[s], 4);       // Q4_0: one arrival per converter warp
             mbar_init(&empty[s], 1 + 4);  // the MMA commit + one per epilogue warp (they read the scales)
         }
         for (int b = 0; b < 2; b++) {
@@ -113,7 +147,8 @@ __global__ void __launch_bounds__(kThreads, 1) matmul_q_tc_kernel(const TcParams
         fence_mbar_init();
     }
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void *)tmem_slot)),
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32((const void *)tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -123,86 +158,90 @@ __global__ void __launch_bounds__(kThreads, 1) matmul_q_tc_kernel(const TcParams
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp >= 5) {  // ---------------------------------------------------------------- producers
-        const int pt = t - 5 * 32;  // 0..127
+    if (warp == 5) {  // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int g = 0; g < nst; g++) {
+                const int s = g % NS;
+                if (g >= NS && !mbar_wait(&empty[s], ((g / NS) - 1) & 1u)) {
+                    raise_error(p.err, kErrMbarTimeout);
+                    *dead = 1;
+                    break;
+                }
+                if (*dead) break;
+                uint8_t *st = sm + s * SB;
+                const int b0 = g * KS;
+                mbar_arrive_tx(&tfull_s[s], stage_tx<DT>());
+                for (int j = 0; j < KS; j++) {
+                    if (DT == QMC_Q8_0) {
+                        tma_2d(st + (2 * j) * kWSlab, &wmap, p.sbytes + (b0 + j) * 32, n0, &tfull_s[s]);
+                        tma_2d(st + (2 * j + 1) * kWSlab, &wmap, p.sbytes + (b0 + j) * 32 + 16, n0, &tfull_s[s]);
+                    } else {
+                        tma_2d(st + kOffRaw + j * kWSlab, &wmap, p.sbytes + (b0 + j) * 16, n0, &tfull_s[s]);
+                    }
+                    tma_2d(st + kOffA + (2 * j) * kASlab, &amap, (b0 + j) * 32, t0, &tfull_s[s]);
+                    tma_2d(st + kOffA + (2 * j + 1) * kASlab, &amap, (b0 + j) * 32 + 16, t0, &tfull_s[s]);
+                }
+                tma_2d(st + kOffDw, &wmap, 16 * (g >> 1), n0, &tfull_s[s]);  // 8 blocks' weight scales per row
+                tma_2d(st + kOffDa, &smap, t0, b0, &tfull_s[s]);             // [KS blocks][NT tokens]
+                issued = g + 1;
+            }
+            // no copy may still be landing when the CTA exits: wait (bounded) for the last stages issued
+            const long long td = clock64();
+            for (int g = issued - 1; g >= 0 && g >= issued - NS; g--)
+                if (!mbar_wait_since(&tfull_s[g % NS], (g / NS) & 1u, td)) {
+                    raise_error(p.err, kErrMbarTimeout);
+                    break;
+                }
+        }
+        __syncwarp();
+    } else if (warp >= 6) {  // ---------------------------------------------------------------- Q4_0 converters
+        const int r = t - 6 * 32;  // weight row of the tile, 0..127
         for (int g = 0; g < nst; g++) {
             const int s = g % NS;
-            if (__any_sync(0xffffffffu, g >= NS && !mbar_wait(&empty[s], ((g / NS) - 1) & 1u))) {
+            if (__any_sync(0xffffffffu, !mbar_wait(&tfull_s[s], (g / NS) & 1u))) {
                 if (lane == 0) raise_error(p.err, kErrMbarTimeout);
                 *dead = 1;
                 break;
             }
             if (__any_sync(0xffffffffu, *dead != 0)) break;
-            uint8_t *st = sm + s * kStage;
-            const int b0 = g * KS;
-            // weight payloads -> int8 core-matrix tiles
-            if (DT == QMC_Q8_0) {
-                for (int i = pt; i < MT * KS * 2; i += 128) {  // 16-byte chunks: row, block, half
-                    const int r = i / (KS * 2), j = (i >> 1) % KS, h = i & 1;
-                    uint4 v = make_uint4(0, 0, 0, 0);
-                    if (n0 + r < p.N && b0 + j < p.nb)
-                        v = __ldg((const uint4 *)(p.W + (n0 + r) * p.wstride + p.sbytes + (int64_t)(b0 + j) * 32 + h * 16));
-                    *(uint4 *)(st + j * kWTile + core_off(r, h)) = v;
-                }
-            } else {
-                for (int i = pt; i < MT * KS; i += 128) {  // one 16-byte nibble block: row, block
-                    const int r = i / KS, j = i % KS;
-                    uint4 v = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // -> 0
-                    if (n0 + r < p.N && b0 + j < p.nb)
-                        v = __ldg((const uint4 *)(p.W + (n0 + r) * p.wstride + p.sbytes + (int64_t)(b0 + j) * 16));
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                    uint32_t o[8];
+            uint8_t *st = sm + s * SB;
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {  // byte q holds element 2q (low nibble) and 2q + 1 (high)
-                        const uint32_t lo = w[k] & 0x0f0f0f0fu, hi = (w[k] >> 4) & 0x0f0f0f0fu;
-                        o[2 * k] = __vsub4(__byte_perm(lo, hi, 0x5140), 0x08080808u);
-                        o[2 * k + 1] = __vsub4(__byte_perm(lo, hi, 0x7362), 0x08080808u);
-                    }
-                    *(uint4 *)(st + j * kWTile + core_off(r, 0)) = make_uint4(o[0], o[1], o[2], o[3]);
-                    *(uint4 *)(st + j * kWTile + core_off(r, 1)) = make_uint4(o[4], o[5], o[6], o[7]);
-                }
-            }
-            {  // weight scales: row pt's KS fp16 scales are 8 aligned bytes
-                float *dw = (float *)(st + kOffDw);
-                uint2 v = make_uint2(0, 0);
-                if (n0 + pt < p.N) v = __ldg((const uint2 *)(p.W + (n0 + pt) * p.wstride + 2 * b0));
-                const uint32_t hw[4] = {v.x & 0xffffu, v.x >> 16, v.y & 0xffffu, v.y >> 16};
+            for (int j = 0; j < KS; j++) {
+                const uint4 v = *(const uint4 *)(st + kOffRaw + j * kWSlab + r * 16);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                uint32_t o[8];
 #pragma unroll
-                for (int j = 0; j < KS; j++) dw[j * MT + pt] = b0 + j < p.nb ? h2f(hw[j]) : 0.0f;
-            }
-            for (int i = pt; i < NT * KS * 2; i += 128) {  // activation blocks
-                const int r = i / (KS * 2), j = (i >> 1) % KS, h = i & 1;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (t0 + r < p.T && b0 + j < p.nb)
-                    v = __ldg((const uint4 *)(p.aq + ((t0 + r) * p.nb + b0 + j) * 32 + h * 16));
-                *(uint4 *)(st + kOffA + j * kATile + core_off(r, h)) = v;
-            }
-            if (pt < NT * KS) {  // activation scales
-                const int r = pt / KS, j = pt % KS;
-                float *da = (float *)(st + kOffDa);
-                da[j * NT + r] = (t0 + r < p.T && b0 + j < p.nb) ? __ldg(p.ad + (t0 + r) * p.nb + b0 + j) : 0.0f;
+                for (int k = 0; k < 4; k++) {  // byte q holds element 2q (low nibble) and 2q + 1 (high)
+                    const uint32_t lo = w[k] & 0x0f0f0f0fu, hi = (w[k] >> 4) & 0x0f0f0f0fu;
+                    o[2 * k] = __vsub4(__byte_perm(lo, hi, 0x5140), 0x08080808u);
+                    o[2 * k + 1] = __vsub4(__byte_perm(lo, hi, 0x7362), 0x08080808u);
+                }
+                *(uint4 *)(st + (2 * j) * kWSlab + r * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                *(uint4 *)(st + (2 * j + 1) * kWSlab + r * 16) = make_uint4(o[4], o[5], o[6], o[7]);
             }
             fence_proxy_async();  // generic-proxy writes -> visible to the tensor core's reads
             __syncwarp();
             if (lane == 0) mbar_arrive(&full[s]);
         }
     } else if (warp == 0) {  // ---------------------------------------------------------------- MMA issuer
-        int issued = 0;  // stages whose MMAs were committed
         if (lane == 0) {
+            int issued = 0;  // stages whose MMAs were committed
             for (int g = 0; g < nst; g++) {
                 const int s = g % NS, buf = g & 1;
-                if (!mbar_wait(&full[s], (g / NS) & 1u) || (g >= 2 && !mbar_wait(&tempty[buf], ((g >> 1) - 1) & 1u))) {
+                uint64_t *ready = DT == QMC_Q4_0 ? &full[s] : &tfull_s[s];
+                if (!mbar_wait(ready, (g / NS) & 1u) || (g >= 2 && !mbar_wait(&tempty[buf], ((g >> 1) - 1) & 1u))) {
                     raise_error(p.err, kErrMbarTimeout);
                     *dead = 1;
                     break;
                 }
                 if (*dead) break;
                 tc_fence_after();
-                const uint8_t *st = sm + s * kStage;
+                const uint8_t *st = sm + s * SB;
                 const int nj = min(KS, p.nb - g * KS);
                 for (int j = 0; j < nj; j++)
-                    mma_i8(tmem + (uint32_t)((buf * KS + j) * NT), smem_desc(st + j * kWTile),
-                           smem_desc(st + kOffA + j * kATile));
+                    mma_i8(tmem + (uint32_t)((buf * KS + j) * NT), smem_desc(st + (2 * j) * kWSlab, kWSlab),
+                           smem_desc(st + kOffA + (2 * j) * kASlab, kASlab));
                 mma_commit(&tfull[buf]);
                 mma_commit(&empty[s]);
                 issued = g + 1;
@@ -229,16 +268,21 @@ __global__ void __launch_bounds__(kThreads, 1) matmul_q_tc_kernel(const TcParams
             }
             if (__any_sync(0xffffffffu, *dead != 0)) break;
             tc_fence_after();
-            const uint8_t *st = sm + s * kStage;
-            const float *dw = (const float *)(st + kOffDw), *da = (const float *)(st + kOffDa);
+            const uint8_t *st = sm + s * SB;
+            const uint2 wsc = *(const uint2 *)(st + kOffDw + row * 16 + 8 * (g & 1));  // this stage's 4 scales
+            const uint32_t hw[4] = {wsc.x & 0xffffu, wsc.x >> 16, wsc.y & 0xffffu, wsc.y >> 16};
+            const float *da = (const float *)(st + kOffDa);
             const int nj = min(KS, p.nb - g * KS);
-            for (int j = 0; j < nj; j++) {
-                uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((buf * KS + j) * NT), r);
-                const float wd = dw[j * MT + row];
 #pragma unroll
-                for (int c = 0; c < NT; c++)
-                    acc[c] = __fadd_rn(acc[c], __fmul_rn((float)(int)r[c], __fmul_rn(wd, da[j * NT + c])));
+            for (int j = 0; j < KS; j++) {
+                if (j < nj) {
+                    uint32_t r[32];
+                    tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((buf * KS + j) * NT), r);
+                    const float wd = h2f(hw[j]);
+#pragma unroll
+                    for (int c = 0; c < NT; c++)
+                        acc[c] = __fadd_rn(acc[c], __fmul_rn((float)(int)r[c], __fmul_rn(wd, da[j * NT + c])));
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -267,33 +311,76 @@ __global__ void __launch_bounds__(kThreads, 1) matmul_q_tc_kernel(const TcParams
     }
 }
 
+// ---------------------------------------------------------------- tensor maps (driver entry point)
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiled)f;
+    });
+    return fn;
+}
+// 2-D row-major map: `cols` elements per row, `rows` rows `pitch` bytes apart; boxes of box_cols x
+// box_rows elements; elements outside the matrix read as zero
+int make_map(CUtensorMap *m, const void *base, CUtensorMapDataType type, int64_t cols, int64_t rows, int64_t pitch,
+             int box_cols, int box_rows) {
+    EncodeTiled fn = encode_fn();
+    if (!fn) return set_error(QMC_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows}, strides[1] = {(cuuint64_t)pitch};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows}, estr[2] = {1, 1};
+    const CUresult r = fn(m, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(QMC_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QMC_OK;
+}
+
+template <int DT>
+int launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const CUtensorMap &smap, const TcParams &p,
+             cudaStream_t s) {
+    int dev = 0;
+    QMC_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(QMC_EINVAL, "matmul_q_tc: device %d out of range", dev);
+    static bool attr_done[64];
+    if (!attr_done[dev]) {
+        QMC_CUDA(cudaFuncSetAttribute(matmul_q_tc_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<DT>()));
+        attr_done[dev] = true;
+    }
+    const dim3 grid((unsigned)((p.N + MT - 1) / MT), (unsigned)((p.T + NT - 1) / NT));
+    matmul_q_tc_kernel<DT><<<grid, 32 * warps<DT>(), smem_bytes<DT>(), s>>>(wmap, amap, smap, p);
+    QMC_LAUNCH_CHECK();
+    return QMC_OK;
+}
+
 }  // namespace
 
-int launch_matmul_q_tc(int dtype, const void *Wsplit, int64_t wstride, const int8_t *aq, const float *ad, float *C,
+int64_t matmul_tc_scale_ld(int64_t T) { return (T + 3) / 4 * 4; }
+
+int launch_matmul_q_tc(int dtype, const void *Wsplit, int64_t wstride, const int8_t *aq, const float *adT, float *C,
                        float *C2, int64_t T, int64_t N, int64_t K, int *err, cudaStream_t s) {
     if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "matmul_q_tc: dtype must be Q8_0 or Q4_0");
-    if (((uintptr_t)Wsplit & 15) || (wstride & 15) || ((uintptr_t)aq & 15))
+    if (((uintptr_t)Wsplit & 15) || (wstride & 15) || ((uintptr_t)aq & 15) || ((uintptr_t)adT & 15))
         return set_error(QMC_EINVAL, "matmul_q_tc: operands must be 16-byte aligned");
     if (C2 && (N & 1)) return set_error(QMC_EINVAL, "matmul_q_tc: split output needs an even row count");
     if (T <= 0 || N <= 0) return QMC_OK;
+    const int64_t nb = nblocks(K);
+    if (wstride > INT32_MAX || N > INT32_MAX || T > INT32_MAX) return set_error(QMC_EINVAL, "matmul_q_tc: too large");
     TcParams p;
-    p.W = (const uint8_t *)Wsplit;
-    p.wstride = wstride;
-    p.sbytes = ((nblocks(K) * 2 + 15) / 16) * 16;
-    p.aq = aq, p.ad = ad, p.C = C, p.C2 = C2, p.T = T, p.N = N, p.nb = (int)nblocks(K), p.err = err;
-    auto fn = dtype == QMC_Q8_0 ? matmul_q_tc_kernel<QMC_Q8_0> : matmul_q_tc_kernel<QMC_Q4_0>;
-    int dev = 0;
-    QMC_CUDA(cudaGetDevice(&dev));
-    static bool attr_done[64][2];
-    if (dev < 0 || dev >= 64) return set_error(QMC_EINVAL, "matmul_q_tc: device %d out of range", dev);
-    if (!attr_done[dev][dtype == QMC_Q4_0]) {
-        QMC_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-        attr_done[dev][dtype == QMC_Q4_0] = true;
-    }
-    dim3 grid((unsigned)((N + MT - 1) / MT), (unsigned)((T + NT - 1) / NT));
-    fn<<<grid, kThreads, kSmem, s>>>(p);
-    QMC_LAUNCH_CHECK();
-    return QMC_OK;
+    p.sbytes = (int)(((nb * 2 + 15) / 16) * 16);
+    p.C = C, p.C2 = C2, p.T = T, p.N = N, p.nb = (int)nb, p.err = err;
+    CUtensorMap wmap, amap, smap;
+    int rc;
+    if ((rc = make_map(&wmap, Wsplit, CU_TENSOR_MAP_DATA_TYPE_UINT8, wstride, N, wstride, 16, MT)) ||
+        (rc = make_map(&amap, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, nb * 32, T, nb * 32, 16, NT)) ||
+        (rc = make_map(&smap, adT, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, T, nb, matmul_tc_scale_ld(T) * 4, NT, KS)))
+        return rc;
+    return dtype == QMC_Q8_0 ? launch_t<QMC_Q8_0>(wmap, amap, smap, p, s) : launch_t<QMC_Q4_0>(wmap, amap, smap, p, s);
 }
 
 }  // namespace qmc

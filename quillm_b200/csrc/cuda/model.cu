@@ -78,7 +78,7 @@ struct qmc_model {
     int pf_cap = 0;
     int *pf_tok = nullptr;
     float *pf_x = nullptr, *pf_xn = nullptr, *pf_qkv = nullptr, *pf_att = nullptr, *pf_c = nullptr, *pf_h = nullptr,
-          *pf_h3 = nullptr, *pf_ad = nullptr;
+          *pf_h3 = nullptr, *pf_ad = nullptr, *pf_adT = nullptr;
     int8_t *pf_aq = nullptr;
     // weight upload: pinned staging buffers (allocated on the first large upload)
     uint8_t *stage[2] = {nullptr, nullptr};
@@ -730,7 +730,8 @@ int prefill_buffers(qmc_model *m, int T) {
         (rc = dalloc(m, (void **)&m->pf_qkv, (size_t)cap * (m->Dl + 2 * m->KVl) * 4)) ||
         (rc = dalloc(m, (void **)&m->pf_att, (size_t)cap * m->Dl * 4)) || (rc = dalloc(m, (void **)&m->pf_c, (size_t)cap * wide * 4)) ||
         (rc = dalloc(m, (void **)&m->pf_h, (size_t)cap * m->Hl * 4)) || (rc = dalloc(m, (void **)&m->pf_h3, (size_t)cap * m->Hl * 4)) ||
-        (rc = dalloc(m, (void **)&m->pf_aq, (size_t)cap * nbk * 32)) || (rc = dalloc(m, (void **)&m->pf_ad, (size_t)cap * nbk * 4)))
+        (rc = dalloc(m, (void **)&m->pf_aq, (size_t)cap * nbk * 32)) || (rc = dalloc(m, (void **)&m->pf_ad, (size_t)cap * nbk * 4)) ||
+        (rc = dalloc(m, (void **)&m->pf_adT, (size_t)matmul_tc_scale_ld(cap) * nbk * 4)))
         return rc;
     m->pf_cap = cap;
     return QMC_OK;
@@ -747,8 +748,8 @@ int prefill_proj(qmc_model *m, int dt, const void *W, const float *A, int T, int
 // w1/w3 matrix's rows 2i / 2i + 1 go to C / C2)
 int prefill_proj_tc(qmc_model *m, int dt, const uint8_t *Ws, const float *A, int T, int64_t N, int64_t K, float *C,
                     float *C2) {
-    RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream));
-    return launch_matmul_q_tc(dt, Ws, split_row_bytes(dt, K), m->pf_aq, m->pf_ad, C, C2, T, N, K, ctx()->err, m->stream);
+    RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream, m->pf_adT, matmul_tc_scale_ld(T)));
+    return launch_matmul_q_tc(dt, Ws, split_row_bytes(dt, K), m->pf_aq, m->pf_adT, C, C2, T, N, K, ctx()->err, m->stream);
 }
 }  // namespace
 
