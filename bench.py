@@ -208,19 +208,26 @@ def time_matvec(qb, torch, dt: int, rows: int, cols: int, iters: int = 64) -> tu
     return sec, algo
 
 
-def time_prefill(qb, torch, T: int, N: int, K: int, iters: int = 10) -> float:
+def time_prefill(qb, torch, T: int, N: int, K: int, iters: int = 10) -> tuple[float, float]:
+    """seconds per launch of the Q8_0 prefill contraction: (tensor cores on the split-row copy, the model's
+    path; CUDA cores on the file layout, qmc_matmul_nt_q)"""
     W = torch.randint(0, 256, (N * row_bytes(Q8_0, K) + 256,), dtype=torch.uint8, device="cuda")
     v = W[: N * row_bytes(Q8_0, K)].view(N, -1, 34)
     v[:, :, 0] = 0x1F
     v[:, :, 1] = 0x21
+    lib = qb.cuda()
+    Ws = torch.empty(N * lib.qmc_split_row_bytes(Q8_0, K) + 256, dtype=torch.uint8, device="cuda")
+    qb.check(lib.qmc_repack_split(Q8_0, W.data_ptr(), N, K, Ws.data_ptr(), None))
     A = torch.randn(T, K, device="cuda")
     Cm = torch.empty(T, N, device="cuda")
-    lib = qb.cuda()
 
-    def launch(stream, i=0):
+    def tc(stream, i=0):
+        qb.check(lib.qmc_matmul_split_q(Q8_0, Ws.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, stream))
+
+    def cc(stream, i=0):
         qb.check(lib.qmc_matmul_nt_q(Q8_0, W.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, stream))
 
-    return _graph_time(torch, launch, iters)
+    return _graph_time(torch, tc, iters), _graph_time(torch, cc, iters)
 
 
 def profile_decode(layers: int) -> None:
@@ -453,12 +460,15 @@ def kernel_sweeps(qb, torch, wl: dict, hbm: float, tflops: float, src: str) -> d
                        "frac": tot_b / tot_t / 1e9 / hbm, "traffic": traffic,
                        "traffic_note": "DRAM bytes per 11008x4096 launch from ncu (algorithmic 25.43 MB)",
                        "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
+    # Q8_0 prefill contraction: tensor cores (tcgen05 kind::i8, the model's batched forward) against the
+    # CUDA-core dp4a kernel; "TOP/s" counts 2 int8 operations per multiply-add
     res["prefill"] = []
     for N, Kd in ((4096, 4096), (11008, 4096)):
         for T in (1, 8, 32, 128, 512):
-            sec = time_prefill(qb, torch, T, N, Kd)
-            res["prefill"].append({"T": T, "N": N, "K": Kd, "tok/s": T / sec, "TFLOP/s": 2 * T * N * Kd / sec / 1e12,
-                                   "us": sec * 1e6})
+            sec, sec_cc = time_prefill(qb, torch, T, N, Kd)
+            res["prefill"].append({"T": T, "N": N, "K": Kd, "kernel": "matmul_q_tc_kernel (tcgen05 kind::i8)",
+                                   "tok/s": T / sec, "TOP/s": 2 * T * N * Kd / sec / 1e12, "us": sec * 1e6,
+                                   "cuda_core_us": sec_cc * 1e6})
     return res
 
 

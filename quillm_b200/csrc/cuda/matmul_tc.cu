@@ -9,13 +9,13 @@
 // order: the tensor cores do the 32 multiply-adds per (row, token, block), the CUDA cores the 4 float
 // operations.
 //
-// Operands reach shared memory by TMA (cp.async.bulk.tensor, 2-D tiles of 16-byte columns), issued by
-// one producer lane up to NS stages ahead.  A stage holds KS blocks.  Each 16-byte column of a block
-// (half h of block j: Q8_0 weight bytes, activation bytes) lands as a slab [rows][16 bytes], which is
-// the no-swizzle K-major core-matrix layout with 8-row groups 128 bytes apart (SBO) and the two halves
-// of a block one slab apart (LBO).  Q4_0 payloads (16 bytes of nibbles per block) land raw and four
-// converter warps expand them to int8 slabs.  The weight scales (the split row's leading fp16 array) and
-// the block-major activation scales arrive by TMA as well.
+// Operands reach shared memory by TMA (cp.async.bulk.tensor), issued by one producer lane up to NS
+// stages ahead.  A stage holds KS = 4 blocks, i.e. 128 bytes of int8 per row: one TMA box per operand
+// lands [rows][128 bytes] with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)),
+// which is the canonical K-major SWIZZLE_128B layout the MMA reads (8-row groups 1024 bytes apart); the
+// MMA of block j starts 32 bytes into the rows.  Q4_0 payloads (16 bytes of nibbles per block) land raw
+// ([rows][64 bytes]) and four converter warps expand them to int8 in the same swizzled layout.  The weight
+// scales (the split row's leading fp16 array) and the block-major activation scales arrive by TMA too.
 //
 // CTA roles: warp 0 allocates TMEM and one lane issues the MMAs; warps 1-4 are the epilogue (warp w may
 // read TMEM lanes 32 (w % 4) .. + 31, the weight rows of that quarter); warp 5 lane 0 issues the TMA
@@ -40,15 +40,16 @@ constexpr int NS = 4;    // stages in the ring
 constexpr int kTmemCols = 2 * KS * NT;  // two buffers of KS block tiles (power of 2, >= 32)
 static_assert(kTmemCols == 256, "TMEM allocation size");
 
-// stage layout (bytes): int8 weight slabs [2 KS][MT][16], activation slabs [2 KS][NT][16], weight scales
-// [MT][16] (8 blocks' fp16 scales per row; this stage's 4 at byte 8 (g & 1)), activation scales [KS][NT]
-// floats, then (Q4_0) raw nibble slabs [KS][MT][16]
-constexpr int kWSlab = MT * 16, kASlab = NT * 16;
-constexpr int kOffA = 2 * KS * kWSlab, kOffDw = kOffA + 2 * KS * kASlab, kOffDa = kOffDw + MT * 16;
+// stage layout (bytes, 1024-aligned tiles): int8 weight tile [MT][128] and activation tile [NT][128]
+// (swizzled), weight scales [MT][16] (8 blocks' fp16 scales per row; this stage's 4 at byte 8 (g & 1)),
+// activation scales [KS][NT] floats, then (Q4_0) the raw nibble payloads [MT][64]
+constexpr int kRow = KS * 32;  // int8 bytes of a row per stage (the 128-byte swizzle span)
+static_assert(kRow == 128, "one stage is one 128-byte swizzle atom wide");
+constexpr int kOffA = MT * kRow, kOffDw = kOffA + NT * kRow, kOffDa = kOffDw + MT * 16;
 constexpr int kOffRaw = kOffDa + KS * NT * 4;
 template <int DT>
 __host__ __device__ constexpr int stage_bytes() {
-    return DT == QMC_Q4_0 ? kOffRaw + KS * kWSlab : kOffRaw;
+    return ((DT == QMC_Q4_0 ? kOffRaw + MT * KS * 16 : kOffRaw) + 1023) / 1024 * 1024;
 }
 template <int DT>
 __host__ __device__ constexpr int warps() {
@@ -56,20 +57,20 @@ __host__ __device__ constexpr int warps() {
 }
 template <int DT>
 __host__ __device__ constexpr int smem_bytes() {
-    return NS * stage_bytes<DT>() + (3 * NS + 4) * 8 + 16;
+    return 1024 + NS * stage_bytes<DT>() + (3 * NS + 4) * 8 + 16;  // + slack to align the tiles to 1024
 }
-static_assert(kOffRaw % 128 == 0 && (kOffRaw + KS * kWSlab) % 128 == 0, "stage alignment");
+static_assert(kOffA % 1024 == 0 && kOffRaw % 128 == 0, "stage alignment");
 // transaction bytes of one stage's TMA copies
 template <int DT>
 __host__ __device__ constexpr uint32_t stage_tx() {
-    return (DT == QMC_Q4_0 ? KS * kWSlab : 2 * KS * kWSlab) + 2 * KS * kASlab + MT * 16 + KS * NT * 4;
+    return (DT == QMC_Q4_0 ? MT * KS * 16 : MT * kRow) + NT * kRow + MT * 16 + KS * NT * 4;
 }
 
-// K-major no-swizzle descriptor: start, LBO (between the two 16-byte halves of a block), SBO 128 (between
-// 8-row groups of a slab), descriptor version 1
-__device__ __forceinline__ uint64_t smem_desc(const void *p, uint32_t lbo) {
+// K-major SWIZZLE_128B descriptor: start (32 bytes further per block inside the atom), LBO 16 bytes
+// (unused by the swizzled K-major form), SBO 1024 (8-row groups of 128-byte rows), version 1
+__device__ __forceinline__ uint64_t smem_desc(const void *p) {
     const uint64_t a = (smem_u32(p) >> 4) & 0x3fffu;
-    return a | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
+    return a | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 // instruction descriptor: s32 accumulator, s8 x s8, both K-major, N = NT, M = MT
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(MT >> 4) << 24);
@@ -121,10 +122,12 @@ struct TcParams {
 
 template <int DT>
 __global__ void __launch_bounds__(32 * warps<DT>(), 1)
-    matmul_q_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap amap,
-                       const __grid_constant__ CUtensorMap smap, const TcParams p) {
+    matmul_q_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dwmap,
+                       const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap smap,
+                       const TcParams p) {
     constexpr int SB = stage_bytes<DT>();
-    extern __shared__ __align__(128) uint8_t sm[];
+    extern __shared__ __align__(128) uint8_t sm_raw[];
+    uint8_t *sm = sm_raw + ((1024 - (smem_u32(sm_raw) & 1023)) & 1023);  // swizzled tiles: 1024-aligned
     uint64_t *tfull_s = (uint64_t *)(sm + NS * SB), *full = tfull_s + NS, *empty = full + NS, *tfull = empty + NS,
              *tempty = tfull + 2;
     volatile uint32_t *tmem_slot = (volatile uint32_t *)(tempty + 2);
@@ -172,17 +175,10 @@ __global__ void __launch_bounds__(32 * warps<DT>(), 1)
                 uint8_t *st = sm + s * SB;
                 const int b0 = g * KS;
                 mbar_arrive_tx(&tfull_s[s], stage_tx<DT>());
-                for (int j = 0; j < KS; j++) {
-                    if (DT == QMC_Q8_0) {
-                        tma_2d(st + (2 * j) * kWSlab, &wmap, p.sbytes + (b0 + j) * 32, n0, &tfull_s[s]);
-                        tma_2d(st + (2 * j + 1) * kWSlab, &wmap, p.sbytes + (b0 + j) * 32 + 16, n0, &tfull_s[s]);
-                    } else {
-                        tma_2d(st + kOffRaw + j * kWSlab, &wmap, p.sbytes + (b0 + j) * 16, n0, &tfull_s[s]);
-                    }
-                    tma_2d(st + kOffA + (2 * j) * kASlab, &amap, (b0 + j) * 32, t0, &tfull_s[s]);
-                    tma_2d(st + kOffA + (2 * j + 1) * kASlab, &amap, (b0 + j) * 32 + 16, t0, &tfull_s[s]);
-                }
-                tma_2d(st + kOffDw, &wmap, 16 * (g >> 1), n0, &tfull_s[s]);  // 8 blocks' weight scales per row
+                if (DT == QMC_Q8_0) tma_2d(st, &wmap, p.sbytes + b0 * 32, n0, &tfull_s[s]);  // [MT][128], swizzled
+                else tma_2d(st + kOffRaw, &wmap, p.sbytes + b0 * 16, n0, &tfull_s[s]);      // [MT][64] raw
+                tma_2d(st + kOffA, &amap, b0 * 32, t0, &tfull_s[s]);            // [NT][128], swizzled
+                tma_2d(st + kOffDw, &dwmap, 16 * (g >> 1), n0, &tfull_s[s]);  // 8 blocks' weight scales per row
                 tma_2d(st + kOffDa, &smap, t0, b0, &tfull_s[s]);             // [KS blocks][NT tokens]
                 issued = g + 1;
             }
@@ -208,7 +204,7 @@ __global__ void __launch_bounds__(32 * warps<DT>(), 1)
             uint8_t *st = sm + s * SB;
 #pragma unroll
             for (int j = 0; j < KS; j++) {
-                const uint4 v = *(const uint4 *)(st + kOffRaw + j * kWSlab + r * 16);
+                const uint4 v = *(const uint4 *)(st + kOffRaw + r * (KS * 16) + j * 16);
                 const uint32_t w[4] = {v.x, v.y, v.z, v.w};
                 uint32_t o[8];
 #pragma unroll
@@ -217,8 +213,9 @@ __global__ void __launch_bounds__(32 * warps<DT>(), 1)
                     o[2 * k] = __vsub4(__byte_perm(lo, hi, 0x5140), 0x08080808u);
                     o[2 * k + 1] = __vsub4(__byte_perm(lo, hi, 0x7362), 0x08080808u);
                 }
-                *(uint4 *)(st + (2 * j) * kWSlab + r * 16) = make_uint4(o[0], o[1], o[2], o[3]);
-                *(uint4 *)(st + (2 * j + 1) * kWSlab + r * 16) = make_uint4(o[4], o[5], o[6], o[7]);
+                // chunks 2j, 2j + 1 of row r, at their 128-byte-swizzle positions
+                *(uint4 *)(st + r * kRow + (((2 * j) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *(uint4 *)(st + r * kRow + (((2 * j + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
             }
             fence_proxy_async();  // generic-proxy writes -> visible to the tensor core's reads
             __syncwarp();
@@ -240,8 +237,7 @@ __global__ void __launch_bounds__(32 * warps<DT>(), 1)
                 const uint8_t *st = sm + s * SB;
                 const int nj = min(KS, p.nb - g * KS);
                 for (int j = 0; j < nj; j++)
-                    mma_i8(tmem + (uint32_t)((buf * KS + j) * NT), smem_desc(st + (2 * j) * kWSlab, kWSlab),
-                           smem_desc(st + kOffA + (2 * j) * kASlab, kASlab));
+                    mma_i8(tmem + (uint32_t)((buf * KS + j) * NT), smem_desc(st + j * 32), smem_desc(st + kOffA + j * 32));
                 mma_commit(&tfull[buf]);
                 mma_commit(&empty[s]);
                 issued = g + 1;
@@ -328,22 +324,23 @@ EncodeTiled encode_fn() {
     return fn;
 }
 // 2-D row-major map: `cols` elements per row, `rows` rows `pitch` bytes apart; boxes of box_cols x
-// box_rows elements; elements outside the matrix read as zero
+// box_rows elements, optionally 128-byte swizzled; elements outside the matrix read as zero
 int make_map(CUtensorMap *m, const void *base, CUtensorMapDataType type, int64_t cols, int64_t rows, int64_t pitch,
-             int box_cols, int box_rows) {
+             int box_cols, int box_rows, bool swizzle = false) {
     EncodeTiled fn = encode_fn();
     if (!fn) return set_error(QMC_ECUDA, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows}, strides[1] = {(cuuint64_t)pitch};
     const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows}, estr[2] = {1, 1};
     const CUresult r = fn(m, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(QMC_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return QMC_OK;
 }
 
 template <int DT>
-int launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const CUtensorMap &smap, const TcParams &p,
-             cudaStream_t s) {
+int launch_t(const CUtensorMap &wmap, const CUtensorMap &dwmap, const CUtensorMap &amap, const CUtensorMap &smap,
+             const TcParams &p, cudaStream_t s) {
     int dev = 0;
     QMC_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return set_error(QMC_EINVAL, "matmul_q_tc: device %d out of range", dev);
@@ -353,7 +350,7 @@ int launch_t(const CUtensorMap &wmap, const CUtensorMap &amap, const CUtensorMap
         attr_done[dev] = true;
     }
     const dim3 grid((unsigned)((p.N + MT - 1) / MT), (unsigned)((p.T + NT - 1) / NT));
-    matmul_q_tc_kernel<DT><<<grid, 32 * warps<DT>(), smem_bytes<DT>(), s>>>(wmap, amap, smap, p);
+    matmul_q_tc_kernel<DT><<<grid, 32 * warps<DT>(), smem_bytes<DT>(), s>>>(wmap, dwmap, amap, smap, p);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }
@@ -374,13 +371,15 @@ int launch_matmul_q_tc(int dtype, const void *Wsplit, int64_t wstride, const int
     TcParams p;
     p.sbytes = (int)(((nb * 2 + 15) / 16) * 16);
     p.C = C, p.C2 = C2, p.T = T, p.N = N, p.nb = (int)nb, p.err = err;
-    CUtensorMap wmap, amap, smap;
+    CUtensorMap wmap, dwmap, amap, smap;
+    const bool q8 = dtype == QMC_Q8_0;
     int rc;
-    if ((rc = make_map(&wmap, Wsplit, CU_TENSOR_MAP_DATA_TYPE_UINT8, wstride, N, wstride, 16, MT)) ||
-        (rc = make_map(&amap, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, nb * 32, T, nb * 32, 16, NT)) ||
+    if ((rc = make_map(&wmap, Wsplit, CU_TENSOR_MAP_DATA_TYPE_UINT8, wstride, N, wstride, q8 ? 128 : KS * 16, MT, q8)) ||
+        (rc = make_map(&dwmap, Wsplit, CU_TENSOR_MAP_DATA_TYPE_UINT8, wstride, N, wstride, 16, MT)) ||
+        (rc = make_map(&amap, aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, nb * 32, T, nb * 32, 128, NT, true)) ||
         (rc = make_map(&smap, adT, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, T, nb, matmul_tc_scale_ld(T) * 4, NT, KS)))
         return rc;
-    return dtype == QMC_Q8_0 ? launch_t<QMC_Q8_0>(wmap, amap, smap, p, s) : launch_t<QMC_Q4_0>(wmap, amap, smap, p, s);
+    return q8 ? launch_t<QMC_Q8_0>(wmap, dwmap, amap, smap, p, s) : launch_t<QMC_Q4_0>(wmap, dwmap, amap, smap, p, s);
 }
 
 }  // namespace qmc
