@@ -267,6 +267,33 @@ def profile_matvec(spec: str) -> None:
     print(f"profile-matvec {spec}: {n} launches ok")
 
 
+def profile_prefill(spec: str) -> None:
+    """--profile-prefill TxNxK:DTYPE[:N]: N launches of the tensor-core prefill contraction (ncu captures)"""
+    import torch
+
+    import quillm_b200 as qb
+
+    shape, dts, *rest = spec.split(":")
+    T, N, K = map(int, shape.split("x"))
+    dt = {"q8_0": Q8_0, "q4_0": Q4_0}[dts]
+    n = int(rest[0]) if rest else 3
+    lib = qb.cuda()
+    qb.check(lib.qmc_set_device(0))
+    rb = row_bytes(dt, K)
+    W = torch.randint(0, 256, (N * rb + 256,), dtype=torch.uint8, device="cuda")
+    v = W[: N * rb].view(N, -1, 34 if dt == Q8_0 else 18)
+    v[:, :, 0] = 0x1F  # fp16 0.01 scales
+    v[:, :, 1] = 0x21
+    Ws = torch.empty(N * lib.qmc_split_row_bytes(dt, K) + 256, dtype=torch.uint8, device="cuda")
+    qb.check(lib.qmc_repack_split(dt, W.data_ptr(), N, K, Ws.data_ptr(), None))
+    A = torch.randn(T, K, device="cuda")
+    Cm = torch.empty(T, N, device="cuda")
+    for _ in range(n):
+        qb.check(lib.qmc_matmul_split_q(dt, Ws.data_ptr(), A.data_ptr(), Cm.data_ptr(), T, N, K, None))
+    qb.check(lib.qmc_sync())
+    print(f"profile-prefill {spec}: {n} launches ok")
+
+
 def traffic_from_profiles(tag: str):
     """DRAM bytes per launch recorded from an ncu capture (profiles/*.md line `traffic[<tag>] = <bytes>`)"""
     pdir = os.path.join(ROOT, "profiles")
@@ -588,7 +615,12 @@ def main():
                     help="only launch N plain matvecs (a small case for ncu captures)")
     ap.add_argument("--profile-decode", type=int, default=None, metavar="LAYERS",
                     help="only decode 134 positions of a Llama-7B-shaped Q4_0 model with LAYERS layers (ncu)")
+    ap.add_argument("--profile-prefill", default=None, metavar="TxNxK:DTYPE[:N]",
+                    help="only launch N tensor-core prefill contractions (a small case for ncu captures)")
     args = ap.parse_args()
+    if args.profile_prefill:
+        profile_prefill(args.profile_prefill)
+        return
     if args.profile_matvec:
         profile_matvec(args.profile_matvec)
         return
