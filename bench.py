@@ -489,11 +489,11 @@ def kernel_sweeps(qb, torch, wl: dict, hbm: float, tflops: float, src: str) -> d
                        "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src}
     # Q8_0 prefill contraction: tensor cores (tcgen05 kind::i8, the model's batched forward) against the
     # CUDA-core dp4a kernel; "TOP/s" counts 2 int8 operations per multiply-add
-    res["prefill"] = []
+    res["prefill_contraction"] = []
     for N, Kd in ((4096, 4096), (11008, 4096)):
         for T in (1, 8, 32, 128, 512):
             sec, sec_cc = time_prefill(qb, torch, T, N, Kd)
-            res["prefill"].append({"T": T, "N": N, "K": Kd, "kernel": "matmul_q_tc_kernel (tcgen05 kind::i8)",
+            res["prefill_contraction"].append({"T": T, "N": N, "K": Kd, "kernel": "matmul_q_tc_kernel (tcgen05 kind::i8)",
                                    "tok/s": T / sec, "TOP/s": 2 * T * N * Kd / sec / 1e12, "us": sec * 1e6,
                                    "cuda_core_us": sec_cc * 1e6})
     return res
