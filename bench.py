@@ -361,24 +361,26 @@ def gpu_arm(args, wl: dict) -> dict | None:
     tok, pos = model.state()
     assert pos == pos0 + K, (pos, pos0, K)
 
-    # e2e: the public per-token call, host buffers, copies inside the timed region
+    # e2e: the public per-token call, host buffers, copies inside the timed region, over the same
+    # positions as the device-timed steps (their cache slots are rewritten), so that both figures carry
+    # the same attention length
     logits = np.zeros(cfg["vocab_size"], np.float32)
-    model.forward(tok, pos, logits)  # warm
+    model.forward(tok, pos0 - 1, logits)  # warm
     d.barrier()
     t0 = time.perf_counter()
     t = tok
     for i in range(K):
-        t = model.forward(t, pos + 1 + i, logits)
+        t = model.forward(t, pos0 + i, logits)
     e2e_s = d.max(time.perf_counter() - t0)
 
     # sampled decoding through the public call: temperature 0.8 / top-p 0.9 drawn on the device, only the
     # 4-byte token copied back per step (the reference's loop copies the logits and samples on the host)
     sampler = qb.Sampler(cfg["vocab_size"], 0.8, 0, 0.9, 1234)
-    t = model.forward_sample(tok, pos, sampler)  # warm
+    t = model.forward_sample(tok, pos0 - 1, sampler)  # warm
     d.barrier()
     t0 = time.perf_counter()
     for i in range(K):
-        t = model.forward_sample(t, pos + 1 + i, sampler)
+        t = model.forward_sample(t, pos0 + i, sampler)
     e2e_sampled_s = d.max(time.perf_counter() - t0)
     sampler.close()
 
