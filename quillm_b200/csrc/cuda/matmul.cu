@@ -38,7 +38,7 @@ __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t T, int6
 }
 
 template <int DT>
-__global__ void __launch_bounds__(256) matmul_q_kernel(const uint8_t *__restrict__ W, const int8_t *__restrict__ aq,
+__global__ void __launch_bounds__(256, 1) matmul_q_kernel(const uint8_t *__restrict__ W, const int8_t *__restrict__ aq,
                                                        const float *__restrict__ ad, float *__restrict__ C, int64_t T,
                                                        int64_t N, int64_t K) {
     __shared__ uint32_t ws[TB * WS], as[TB * WS];
