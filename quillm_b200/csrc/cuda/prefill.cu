@@ -62,66 +62,102 @@ __global__ void rope_kv_rows_kernel(float *__restrict__ qkv, int Dq, int KVl, in
         kv_st2(vc, kv16, (int64_t)pos * KVl + 2 * i, row[Dq + KVl + 2 * i], row[Dq + KVl + 2 * i + 1]);
 }
 
-// one warp per (query head, token): lane l holds q[l + 32 j] (j < 4, head_dim <= 128); the positions are
-// walked 4 at a time with the 4 score reductions interleaved, online softmax (running max, sum, and
-// accumulator rescaled when the max grows)
-constexpr int kPfWarps = 4;  // tokens per block
-template <typename KT>         // cache element: float or __half
-__global__ void __launch_bounds__(32 * kPfWarps) attn_prefill_kernel(const float *__restrict__ qkv, int64_t T, int64_t ldq,
-                                                                   int group, int hd, int KVl, int pos0, float scale,
-                                                                   const KT *__restrict__ kc,
-                                                                   const KT *__restrict__ vc, float *__restrict__ out) {
-    const int lane = threadIdx.x & 31;
-    const int64_t t = (int64_t)blockIdx.x * kPfWarps + (threadIdx.x >> 5);
-    if (t >= T) return;
+// Causal attention of a tile of kQT query tokens of one head: the head's K and V rows are staged through
+// shared memory kPT positions at a time and shared by the tile's tokens.  Each warp owns kQT / 4 tokens.
+// Per token and position tile, lane p scores position p (its dot over head_dim, K transposed in shared
+// memory so lane p reads its own column), the warp updates the online softmax once for the tile (max,
+// one rescale of the running sum and accumulator), and lane l accumulates head dimensions 4l .. 4l + 3
+// over the tile's positions.  Rows are zero-padded to a multiple of 4 dimensions in shared memory.
+constexpr int kQT = 32, kPT = 32;  // query tokens per block, positions per staged tile
+template <typename KT>             // cache element: float or __half
+__global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const float *__restrict__ qkv, int64_t T, int64_t ldq, int group,
+                                                           int hd, int KVl, int pos0, float scale,
+                                                           const KT *__restrict__ kc, const KT *__restrict__ vc,
+                                                           float *__restrict__ out) {
+    extern __shared__ __align__(16) float smf[];
+    const int hd4 = (hd + 3) & ~3;
+    float *Kt = smf;                 // [hd4 / 4][kPT][4]: dims 4c .. 4c + 3 of position p at (c * kPT + p) * 4
+    float *Vs = Kt + hd4 * kPT;      // [kPT][hd4]
+    float *Qs = Vs + kPT * hd4;      // [kQT][hd4]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int h = blockIdx.y, kvh = h / group;
-    const int npos = pos0 + (int)t + 1;
-    float q[4], o[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int d = lane + 32 * j;
-        q[j] = d < hd ? qkv[t * ldq + (int64_t)h * hd + d] : 0.0f;
-        o[j] = 0.0f;
+    const int64_t tq0 = (int64_t)blockIdx.x * kQT;
+    const int nq = (int)(T - tq0 < kQT ? T - tq0 : kQT);
+    for (int i = tid; i < kQT * hd4; i += 128) {
+        const int r = i / hd4, d = i % hd4;
+        Qs[i] = (r < nq && d < hd) ? qkv[(tq0 + r) * ldq + (int64_t)h * hd + d] : 0.0f;
     }
+    constexpr int TW = kQT / 4;  // tokens per warp
+    float m[TW], l[TW], o[TW][4];
+#pragma unroll
+    for (int j = 0; j < TW; j++) {
+        m[j] = -INFINITY, l[j] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[j][i] = 0.0f;
+    }
+    const int last = pos0 + (int)tq0 + nq - 1;  // the tile's last token sees positions 0 .. last
     const KT *kb = kc + (int64_t)kvh * hd, *vb = vc + (int64_t)kvh * hd;
-    float m = -INFINITY, l = 0.0f;
-    for (int p0 = 0; p0 < npos; p0 += 4) {
-        float sc[4], v[4][4];  // the 4 positions' K and V rows are loaded together
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int p = p0 + c;
-            float s = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int d = lane + 32 * j;
-                const bool ok = p < npos && d < hd;
-                if (ok) s = fmaf(q[j], kv_ld(kb + (int64_t)p * KVl + d), s);
-                v[c][j] = ok ? kv_ld(vb + (int64_t)p * KVl + d) : 0.0f;
-            }
-            sc[c] = s;
+    for (int p0 = 0; p0 <= last; p0 += kPT) {
+        __syncthreads();  // the previous tile's K/V (and, first time, nothing) are no longer read
+        for (int i = tid; i < kPT * hd4; i += 128) {
+            const int pp = i / hd4, d = i % hd4, pos = p0 + pp;
+            const bool ok = pos <= last && d < hd;
+            Kt[((d >> 2) * kPT + pp) * 4 + (d & 3)] = ok ? kv_ld(kb + (int64_t)pos * KVl + d) : 0.0f;
+            Vs[pp * hd4 + d] = ok ? kv_ld(vb + (int64_t)pos * KVl + d) : 0.0f;
         }
+        __syncthreads();
 #pragma unroll
-        for (int off = 16; off; off >>= 1)
+        for (int j = 0; j < TW; j++) {
+            const int r = warp * TW + j;  // query token of the tile
+            if (r >= nq) break;
+            const int lim = pos0 + (int)tq0 + r;  // causal: positions 0 .. lim
+            if (p0 > lim) continue;
+            const float *q = Qs + r * hd4;
+            float sc = 0.0f;
+            for (int c = 0; c < hd4 / 4; c++) {
+                const float4 kv4 = *(const float4 *)(Kt + (c * kPT + lane) * 4);
+                const float4 q4 = *(const float4 *)(q + 4 * c);
+                sc = fmaf(q4.x, kv4.x, sc);
+                sc = fmaf(q4.y, kv4.y, sc);
+                sc = fmaf(q4.z, kv4.z, sc);
+                sc = fmaf(q4.w, kv4.w, sc);
+            }
+            sc = p0 + lane <= lim ? sc * scale : -INFINITY;
+            float mx = sc;
 #pragma unroll
-            for (int c = 0; c < 4; c++) sc[c] += __shfl_xor_sync(0xffffffffu, sc[c], off);
+            for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[j], mx);
+            const float corr = expf(m[j] - mn), e = expf(sc - mn);  // e = 0 past the causal limit
+            float es = e;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int p = p0 + c;
-            if (p >= npos) break;
-            const float s = sc[c] * scale;
-            const float mn = fmaxf(m, s);
-            const float corr = expf(m - mn), e = expf(s - mn);
-            l = l * corr + e;
+            for (int off = 16; off; off >>= 1) es += __shfl_xor_sync(0xffffffffu, es, off);
+            l[j] = l[j] * corr + es;
+            m[j] = mn;
 #pragma unroll
-            for (int j = 0; j < 4; j++) o[j] = o[j] * corr + e * v[c][j];
-            m = mn;
+            for (int i = 0; i < 4; i++) o[j][i] *= corr;
+            const bool own = 4 * lane < hd4;  // this lane holds head dimensions
+            for (int pp = 0; pp < kPT; pp++) {
+                const float ep = __shfl_sync(0xffffffffu, e, pp);  // every lane takes part
+                if (own) {
+                    const float4 v4 = *(const float4 *)(Vs + pp * hd4 + 4 * lane);
+                    o[j][0] = fmaf(ep, v4.x, o[j][0]);
+                    o[j][1] = fmaf(ep, v4.y, o[j][1]);
+                    o[j][2] = fmaf(ep, v4.z, o[j][2]);
+                    o[j][3] = fmaf(ep, v4.w, o[j][3]);
+                }
+            }
         }
     }
-    const float rl = 1.0f / l;
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int d = lane + 32 * j;
-        if (d < hd) out[t * (int64_t)gridDim.y * hd + (int64_t)h * hd + d] = o[j] * rl;
+    for (int j = 0; j < TW; j++) {
+        const int r = warp * TW + j;
+        if (r >= nq) break;
+        const float rl = 1.0f / l[j];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int d = 4 * lane + i;
+            if (d < hd) out[(tq0 + r) * (int64_t)gridDim.y * hd + (int64_t)h * hd + d] = o[j][i] * rl;
+        }
     }
 }
 
@@ -156,13 +192,18 @@ int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0
 int launch_attn_prefill(const float *qkv, int64_t T, int64_t ldq, int n_heads, int group, int hd, int KVl, int pos0,
                         float scale, const void *kc, const void *vc, bool kv16, float *out, cudaStream_t s) {
     if (hd > 128) return set_error(QMC_EINVAL, "prefill attention: head_dim %d > 128", hd);
-    dim3 grid((unsigned)((T + kPfWarps - 1) / kPfWarps), (unsigned)n_heads);
-    if (kv16)
-        attn_prefill_kernel<<<grid, 32 * kPfWarps, 0, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const __half *)kc,
-                                                           (const __half *)vc, out);
-    else
-        attn_prefill_kernel<<<grid, 32 * kPfWarps, 0, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const float *)kc,
-                                                           (const float *)vc, out);
+    const int hd4 = (hd + 3) & ~3;
+    const size_t smem = (size_t)(hd4 * kPT + kPT * hd4 + kQT * hd4) * 4;
+    dim3 grid((unsigned)((T + kQT - 1) / kQT), (unsigned)n_heads);
+    if (kv16) {
+        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attn_prefill_kernel<<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const __half *)kc,
+                                                    (const __half *)vc, out);
+    } else {
+        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attn_prefill_kernel<<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const float *)kc,
+                                                    (const float *)vc, out);
+    }
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }
