@@ -294,6 +294,21 @@ def profile_prefill(spec: str) -> None:
     print(f"profile-prefill {spec}: {n} launches ok")
 
 
+def profile_prompt(T: int) -> None:
+    """--profile-prompt T: the 7B Q4_0 model's batched forward of a T-token prompt, twice (ncu launch lists)"""
+    import quillm_b200 as qb
+
+    wl = WORKLOADS["llama7b_q4_0"]
+    qb.check(qb.cuda().qmc_set_device(0))
+    m = qb.Model(dict(wl["cfg"]))
+    m.synthesize(wl["dtype"], wl["seed"], STD)
+    prompt = np.random.default_rng(wl["seed"] + 2000).integers(3, wl["cfg"]["vocab_size"], T).astype(np.int32)
+    for _ in range(2):
+        m.prefill(prompt, 0)
+    m.close()
+    print(f"profile-prompt {T}: 2 prefills ok")
+
+
 def traffic_from_profiles(tag: str):
     """DRAM bytes per launch recorded from an ncu capture (profiles/*.md line `traffic[<tag>] = <bytes>`)"""
     pdir = os.path.join(ROOT, "profiles")
@@ -625,7 +640,12 @@ def main():
                     help="only decode 134 positions of a Llama-7B-shaped Q4_0 model with LAYERS layers (ncu)")
     ap.add_argument("--profile-prefill", default=None, metavar="TxNxK:DTYPE[:N]",
                     help="only launch N tensor-core prefill contractions (a small case for ncu captures)")
+    ap.add_argument("--profile-prompt", type=int, default=None, metavar="T",
+                    help="only run the 7B Q4_0 model's batched forward of a T-token prompt twice (ncu)")
     args = ap.parse_args()
+    if args.profile_prompt:
+        profile_prompt(args.profile_prompt)
+        return
     if args.profile_prefill:
         profile_prefill(args.profile_prefill)
         return

@@ -746,10 +746,16 @@ int prefill_proj(qmc_model *m, int dt, const void *W, const float *A, int T, int
 }
 // the same on the tensor cores, from the split-row copy the decode kernel streams (C2: an interleaved
 // w1/w3 matrix's rows 2i / 2i + 1 go to C / C2)
+// A null: the activation blocks are already in pf_aq / pf_adT (rmsnorm fused with the quantization)
 int prefill_proj_tc(qmc_model *m, int dt, const uint8_t *Ws, const float *A, int T, int64_t N, int64_t K, float *C,
                     float *C2) {
-    RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream, m->pf_adT, matmul_tc_scale_ld(T)));
+    if (A) RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream, m->pf_adT, matmul_tc_scale_ld(T)));
     return launch_matmul_q_tc(dt, Ws, split_row_bytes(dt, K), m->pf_aq, m->pf_adT, C, C2, T, N, K, ctx()->err, m->stream);
+}
+// rmsnorm(x) * w straight into the activation blocks of the next tensor-core contraction
+int prefill_norm_quant(qmc_model *m, const float *w, int T) {
+    return launch_rmsnorm_quant_rows(m->pf_x, w, T, m->D, m->cfg.norm_eps, m->pf_aq, m->pf_ad, m->pf_adT,
+                                     matmul_tc_scale_ld(T), m->stream);
 }
 }  // namespace
 
@@ -774,19 +780,24 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     for (int l = 0; l < m->L; l++) {
         Layer &Ly = m->layers[l];
         void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
-        RC(launch_rmsnorm_rows(m->pf_x, Ly.attn_norm, m->pf_xn, n, D, eps, s));
-        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WQ], Ly.sqkv, m->pf_xn, n, NQKV, D, m->pf_qkv, nullptr));
-        else RC(prefill_proj(m, Ly.dt[QMC_T_WQ], Ly.wqkv, m->pf_xn, n, NQKV, D, m->pf_qkv));
+        if (tc) {
+            RC(prefill_norm_quant(m, Ly.attn_norm, n));
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_WQ], Ly.sqkv, nullptr, n, NQKV, D, m->pf_qkv, nullptr));
+        } else {
+            RC(launch_rmsnorm_rows(m->pf_x, Ly.attn_norm, m->pf_xn, n, D, eps, s));
+            RC(prefill_proj(m, Ly.dt[QMC_T_WQ], Ly.wqkv, m->pf_xn, n, NQKV, D, m->pf_qkv));
+        }
         RC(launch_rope_kv_rows(m->pf_qkv, n, Dq, KVl, m->hd, pos0, m->rope, kcl, vcl, m->kv16 != 0, s));
         RC(launch_attn_prefill(m->pf_qkv, n, NQKV, m->NHl, m->NH / m->NKV, m->hd, KVl, pos0, 1.0f / sqrtf((float)m->hd), kcl,
                                vcl, m->kv16 != 0, m->pf_att, s));
         if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WO], Ly.swo, m->pf_att, n, D, Dq, m->pf_c, nullptr));
         else RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
         RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
-        RC(launch_rmsnorm_rows(m->pf_x, Ly.ffn_norm, m->pf_xn, n, D, eps, s));
         if (tc) {
-            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.s13, m->pf_xn, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
+            RC(prefill_norm_quant(m, Ly.ffn_norm, n));
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.s13, nullptr, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
         } else {
+            RC(launch_rmsnorm_rows(m->pf_x, Ly.ffn_norm, m->pf_xn, n, D, eps, s));
             RC(prefill_proj(m, Ly.dt[QMC_T_W1], Ly.w1, m->pf_xn, n, H, D, m->pf_h));
             RC(prefill_proj(m, Ly.dt[QMC_T_W3], Ly.w3, m->pf_xn, n, H, D, m->pf_h3));
         }

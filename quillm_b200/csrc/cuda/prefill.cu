@@ -38,6 +38,44 @@ __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__
     for (int64_t i = t; i < n; i += blockDim.x) yr[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
+// rmsnorm of one row per block followed by its Q8_0 quantization, without the normalised row in memory:
+// the same operations as rmsnorm_rows then quantize_act (inv from the double sum of squares, v = (x * inv)
+// * w rounded twice, per 32-element block the reference's quantizer), so the blocks are bit-identical
+__global__ void rmsnorm_quant_rows_kernel(const float *__restrict__ x, const float *__restrict__ w, int64_t n, float eps,
+                                          int8_t *__restrict__ qs, float *__restrict__ d, float *__restrict__ dT,
+                                          int64_t ldT) {
+    __shared__ double red[32];
+    __shared__ float inv_s;
+    const int64_t row = blockIdx.x;
+    const float *xr = x + row * n;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    double ss = 0.0;
+    for (int64_t i = t; i < n; i += blockDim.x) ss = fma((double)xr[i], (double)xr[i], ss);
+    ss = warp_sum_d(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (t == 0) {
+        double tot = 0.0;
+        for (int k = 0; k < (int)(blockDim.x >> 5); k++) tot += red[k];
+        inv_s = (float)(1.0 / sqrt(tot / (double)n + (double)eps));
+    }
+    __syncthreads();
+    const float inv = inv_s;
+    const int64_t nb = nblocks(n);
+    for (int64_t b = warp; b < nb; b += blockDim.x >> 5) {
+        const int64_t c = b * 32 + lane;
+        const float v = c < n ? __fmul_rn(__fmul_rn(xr[c], inv), w[c]) : 0.0f;
+        float dd;
+        uint32_t dh;
+        const int q = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
+        qs[row * nb * 32 + c] = (int8_t)q;
+        if (lane == 0) {
+            d[row * nb + b] = dd;
+            if (dT) dT[b * ldT + row] = dd;
+        }
+    }
+}
+
 // p0 = x0 c - x1 s ; p1 = x0 s + x1 c, each product and sum rounded separately (src/ops.c:121-123)
 __device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &o0, float &o1) {
     o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
@@ -113,15 +151,16 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const float *__res
             const int lim = pos0 + (int)tq0 + r;  // causal: positions 0 .. lim
             if (p0 > lim) continue;
             const float *q = Qs + r * hd4;
-            float sc = 0.0f;
+            float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four independent chains, summed at the end
             for (int c = 0; c < hd4 / 4; c++) {
                 const float4 kv4 = *(const float4 *)(Kt + (c * kPT + lane) * 4);
                 const float4 q4 = *(const float4 *)(q + 4 * c);
-                sc = fmaf(q4.x, kv4.x, sc);
-                sc = fmaf(q4.y, kv4.y, sc);
-                sc = fmaf(q4.z, kv4.z, sc);
-                sc = fmaf(q4.w, kv4.w, sc);
+                s4[0] = fmaf(q4.x, kv4.x, s4[0]);
+                s4[1] = fmaf(q4.y, kv4.y, s4[1]);
+                s4[2] = fmaf(q4.z, kv4.z, s4[2]);
+                s4[3] = fmaf(q4.w, kv4.w, s4[3]);
             }
+            float sc = (s4[0] + s4[1]) + (s4[2] + s4[3]);
             sc = p0 + lane <= lim ? sc * scale : -INFINITY;
             float mx = sc;
 #pragma unroll
@@ -182,6 +221,13 @@ int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, i
     return QMC_OK;
 }
 
+int launch_rmsnorm_quant_rows(const float *x, const float *w, int64_t T, int64_t n, float eps, int8_t *qs, float *d,
+                              float *dT, int64_t ldT, cudaStream_t s) {
+    rmsnorm_quant_rows_kernel<<<(unsigned)T, 256, 0, s>>>(x, w, n, eps, qs, d, dT, ldT);
+    QMC_LAUNCH_CHECK();
+    return QMC_OK;
+}
+
 int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0, const float2 *rope, void *kc,
                         void *vc, bool kv16, cudaStream_t s) {
     rope_kv_rows_kernel<<<(unsigned)T, 256, 0, s>>>(qkv, Dq, KVl, hd, pos0, rope, kc, vc, kv16);
@@ -195,12 +241,20 @@ int launch_attn_prefill(const float *qkv, int64_t T, int64_t ldq, int n_heads, i
     const int hd4 = (hd + 3) & ~3;
     const size_t smem = (size_t)(hd4 * kPT + kPT * hd4 + kQT * hd4) * 4;
     dim3 grid((unsigned)((T + kQT - 1) / kQT), (unsigned)n_heads);
+    int dev = 0;
+    QMC_CUDA(cudaGetDevice(&dev));
+    static bool attr_done[64];
+    if (dev < 0 || dev >= 64) return set_error(QMC_EINVAL, "prefill attention: device %d out of range", dev);
+    if (!attr_done[dev]) {  // the largest tile set (head_dim 128)
+        const int most = 3 * 128 * kPT * 4;
+        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+        attr_done[dev] = true;
+    }
     if (kv16) {
-        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attn_prefill_kernel<<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const __half *)kc,
                                                     (const __half *)vc, out);
     } else {
-        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attn_prefill_kernel<<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const float *)kc,
                                                     (const float *)vc, out);
     }

@@ -10,6 +10,10 @@ namespace qmc {
 int launch_embed_rows(int dtype, const void *table, int64_t cols, const int *tokens, int64_t T, float *x, cudaStream_t s);
 // out[t] = rmsnorm(x[t]) * w, per row as src/ops.c:93-98
 int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, int64_t n, float eps, cudaStream_t s);
+// the Q8_0 blocks (qs [T][nb*32], scales d [T][nb] and, with dT, dT[b * ldT + t]) of rmsnorm(x[t]) * w: the
+// same bits as launch_rmsnorm_rows followed by launch_quantize_act, in one pass
+int launch_rmsnorm_quant_rows(const float *x, const float *w, int64_t T, int64_t n, float eps, int8_t *qs, float *d,
+                              float *dT, int64_t ldT, cudaStream_t s);
 // rows of qkv[T][Dq + 2 KVl] at positions pos0 + t: RoPE on the q pairs (in place) and the k pairs, then
 // k and v stored in the layer's cache slots [pos][KVl] of float, or of __half when kv16
 // (src/model.c:165-173, src/ops.c:114-126)
