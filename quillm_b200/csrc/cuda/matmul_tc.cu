@@ -36,7 +36,12 @@ namespace {
 constexpr int MT = 128;  // weight rows per CTA (MMA M: TMEM lanes)
 constexpr int NT = 32;   // tokens per CTA (MMA N)
 constexpr int KS = 4;    // blocks per stage
-constexpr int NS = 4;    // stages in the ring
+// stages in the ring: 4 for Q8_0; 3 for Q4_0, whose stages also hold the raw nibbles, so that two CTAs
+// still fit on an SM
+template <int DT>
+__host__ __device__ constexpr int ring() {
+    return DT == QMC_Q4_0 ? 3 : 4;
+}
 constexpr int kTmemCols = 2 * KS * NT;  // two buffers of KS block tiles (power of 2, >= 32)
 static_assert(kTmemCols == 256, "TMEM allocation size");
 
@@ -57,7 +62,7 @@ __host__ __device__ constexpr int warps() {
 }
 template <int DT>
 __host__ __device__ constexpr int smem_bytes() {
-    return 1024 + NS * stage_bytes<DT>() + (3 * NS + 4) * 8 + 16;  // + slack to align the tiles to 1024
+    return 1024 + ring<DT>() * stage_bytes<DT>() + (3 * ring<DT>() + 4) * 8 + 16;  // + slack to align the tiles
 }
 static_assert(kOffA % 1024 == 0 && kOffRaw % 128 == 0, "stage alignment");
 // transaction bytes of one stage's TMA copies
@@ -121,11 +126,11 @@ struct TcParams {
 };
 
 template <int DT>
-__global__ void __launch_bounds__(32 * warps<DT>(), 1)
+__global__ void __launch_bounds__(32 * warps<DT>(), 2)
     matmul_q_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dwmap,
                        const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap smap,
                        const TcParams p) {
-    constexpr int SB = stage_bytes<DT>();
+    constexpr int SB = stage_bytes<DT>(), NS = ring<DT>();
     extern __shared__ __align__(128) uint8_t sm_raw[];
     uint8_t *sm = sm_raw + ((1024 - (smem_u32(sm_raw) & 1023)) & 1023);  // swizzled tiles: 1024-aligned
     uint64_t *tfull_s = (uint64_t *)(sm + NS * SB), *full = tfull_s + NS, *empty = full + NS, *tfull = empty + NS,
