@@ -801,9 +801,13 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
             RC(prefill_proj(m, Ly.dt[QMC_T_W1], Ly.w1, m->pf_xn, n, H, D, m->pf_h));
             RC(prefill_proj(m, Ly.dt[QMC_T_W3], Ly.w3, m->pf_xn, n, H, D, m->pf_h3));
         }
-        RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
-        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_W2], Ly.sw2, m->pf_h, n, D, H, m->pf_c, nullptr));
-        else RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
+        if (tc) {  // SwiGLU straight into the w2 contraction's activation blocks
+            RC(launch_swiglu_quant_rows(m->pf_h, m->pf_h3, n, H, m->pf_aq, m->pf_ad, m->pf_adT, matmul_tc_scale_ld(n), s));
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W2], Ly.sw2, nullptr, n, D, H, m->pf_c, nullptr));
+        } else {
+            RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
+            RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
+        }
         RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
     }
     // logits of the last token: the output GEMV with the final rmsnorm fused, as a decode step's

@@ -76,6 +76,32 @@ __global__ void rmsnorm_quant_rows_kernel(const float *__restrict__ x, const flo
     }
 }
 
+// h = silu(g) * u over T rows of n (the SwiGLU of src/ops.c:128-133, same roundings as swiglu_kernel)
+// straight into its Q8_0 blocks: warp per 32-element block, h never stored
+__global__ void swiglu_quant_rows_kernel(const float *__restrict__ g, const float *__restrict__ u, int64_t T, int64_t n,
+                                         int8_t *__restrict__ qs, float *__restrict__ d, float *__restrict__ dT,
+                                         int64_t ldT) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nb = nblocks(n);
+    const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t blk = w0; blk < T * nb; blk += nw) {
+        const int64_t t = blk / nb, b = blk % nb, c = b * 32 + lane;
+        float v = 0.0f;
+        if (c < n) {
+            const float gv = g[t * n + c];
+            v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[t * n + c]);
+        }
+        float dd;
+        uint32_t dh;
+        const int q = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
+        qs[t * nb * 32 + c] = (int8_t)q;
+        if (lane == 0) {
+            d[t * nb + b] = dd;
+            if (dT) dT[b * ldT + t] = dd;
+        }
+    }
+}
+
 // p0 = x0 c - x1 s ; p1 = x0 s + x1 c, each product and sum rounded separately (src/ops.c:121-123)
 __device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &o0, float &o1) {
     o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
@@ -107,6 +133,13 @@ __global__ void rope_kv_rows_kernel(float *__restrict__ qkv, int Dq, int KVl, in
 // one rescale of the running sum and accumulator), and lane l accumulates head dimensions 4l .. 4l + 3
 // over the tile's positions.  Rows are zero-padded to a multiple of 4 dimensions in shared memory.
 constexpr int kQT = 32, kPT = 32;  // query tokens per block, positions per staged tile
+// four consecutive cache elements (16-byte aligned for float, 8-byte for __half)
+__device__ __forceinline__ float4 kv_ld4(const float *p) { return __ldcg((const float4 *)p); }
+__device__ __forceinline__ float4 kv_ld4(const __half *p) {
+    const uint2 r = __ldcg((const uint2 *)p);
+    const float2 a = __half22float2(*(const __half2 *)&r.x), b = __half22float2(*(const __half2 *)&r.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+}
 template <typename KT>             // cache element: float or __half
 __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const float *__restrict__ qkv, int64_t T, int64_t ldq, int group,
                                                            int hd, int KVl, int pos0, float scale,
@@ -134,14 +167,28 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const float *__res
         for (int i = 0; i < 4; i++) o[j][i] = 0.0f;
     }
     const int last = pos0 + (int)tq0 + nq - 1;  // the tile's last token sees positions 0 .. last
+    const bool vec = (hd & 3) == 0 && (KVl & 3) == 0;  // 4-dimension groups stay aligned in the cache
     const KT *kb = kc + (int64_t)kvh * hd, *vb = vc + (int64_t)kvh * hd;
     for (int p0 = 0; p0 <= last; p0 += kPT) {
         __syncthreads();  // the previous tile's K/V (and, first time, nothing) are no longer read
-        for (int i = tid; i < kPT * hd4; i += 128) {
-            const int pp = i / hd4, d = i % hd4, pos = p0 + pp;
-            const bool ok = pos <= last && d < hd;
-            Kt[((d >> 2) * kPT + pp) * 4 + (d & 3)] = ok ? kv_ld(kb + (int64_t)pos * KVl + d) : 0.0f;
-            Vs[pp * hd4 + d] = ok ? kv_ld(vb + (int64_t)pos * KVl + d) : 0.0f;
+        if (vec) {  // 4 dimensions per load; K positions vary fastest (conflict-free transposed stores)
+            for (int i = tid; i < kPT * (hd4 / 4); i += 128) {
+                const int pp = i % kPT, c = i / kPT, pos = p0 + pp;
+                *(float4 *)(Kt + (c * kPT + pp) * 4) = pos <= last ? kv_ld4(kb + (int64_t)pos * KVl + 4 * c)
+                                                                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+            for (int i = tid; i < kPT * (hd4 / 4); i += 128) {
+                const int c = i % (hd4 / 4), pp = i / (hd4 / 4), pos = p0 + pp;
+                *(float4 *)(Vs + pp * hd4 + 4 * c) = pos <= last ? kv_ld4(vb + (int64_t)pos * KVl + 4 * c)
+                                                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+        } else {
+            for (int i = tid; i < kPT * hd4; i += 128) {
+                const int pp = i / hd4, d = i % hd4, pos = p0 + pp;
+                const bool ok = pos <= last && d < hd;
+                Kt[((d >> 2) * kPT + pp) * 4 + (d & 3)] = ok ? kv_ld(kb + (int64_t)pos * KVl + d) : 0.0f;
+                Vs[pp * hd4 + d] = ok ? kv_ld(vb + (int64_t)pos * KVl + d) : 0.0f;
+            }
         }
         __syncthreads();
 #pragma unroll
@@ -224,6 +271,15 @@ int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, i
 int launch_rmsnorm_quant_rows(const float *x, const float *w, int64_t T, int64_t n, float eps, int8_t *qs, float *d,
                               float *dT, int64_t ldT, cudaStream_t s) {
     rmsnorm_quant_rows_kernel<<<(unsigned)T, 256, 0, s>>>(x, w, n, eps, qs, d, dT, ldT);
+    QMC_LAUNCH_CHECK();
+    return QMC_OK;
+}
+
+int launch_swiglu_quant_rows(const float *g, const float *u, int64_t T, int64_t n, int8_t *qs, float *d, float *dT,
+                             int64_t ldT, cudaStream_t s) {
+    const int64_t warps = T * nblocks(n);
+    const int64_t grid = (warps * 32 + 255) / 256;
+    swiglu_quant_rows_kernel<<<(int)(grid < 65535 ? grid : 65535), 256, 0, s>>>(g, u, T, n, qs, d, dT, ldT);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }

@@ -14,6 +14,9 @@ int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, i
 // same bits as launch_rmsnorm_rows followed by launch_quantize_act, in one pass
 int launch_rmsnorm_quant_rows(const float *x, const float *w, int64_t T, int64_t n, float eps, int8_t *qs, float *d,
                               float *dT, int64_t ldT, cudaStream_t s);
+// the Q8_0 blocks of silu(g[t]) * u[t] (the SwiGLU rows, same bits as launch_swiglu then launch_quantize_act)
+int launch_swiglu_quant_rows(const float *g, const float *u, int64_t T, int64_t n, int8_t *qs, float *d, float *dT,
+                             int64_t ldT, cudaStream_t s);
 // rows of qkv[T][Dq + 2 KVl] at positions pos0 + t: RoPE on the q pairs (in place) and the k pairs, then
 // k and v stored in the layer's cache slots [pos][KVl] of float, or of __half when kv16
 // (src/model.c:165-173, src/ops.c:114-126)
