@@ -10,7 +10,7 @@ files that pin the hot path into this directory:
   *.ref.f32 / *.reffp.f32 / *.tokens    (.ref) and on the original fp32 weights (.reffp), 20 positions
   l2c_f32.*                             llama2.c-converted model case (gen_fixtures.py:46-54)
 
-Usage:  python tests/golden/make_golden.py [REFERENCE_ROOT]     (needs the reference checkout;
+Usage:  python tests/golden/make_golden.py REFERENCE_ROOT     (needs the reference checkout;
 the committed fixtures are what the tests read, so the GPU box never needs the reference).
 """
 import importlib.util
@@ -40,4 +40,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py REFERENCE_ROOT (the reference checkout)")
+    main(sys.argv[1])
