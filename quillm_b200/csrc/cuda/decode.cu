@@ -108,7 +108,9 @@ __device__ __forceinline__ unsigned long long *trace_slot(int ph, int k) {
 #endif
 }
 // CTA 0 also records every stage g < kTrStages: [g][0] issued, [1] consumer saw it full, [2] released
+#ifdef QMC_DECODE_TRACE
 constexpr int kTrStages = 4096;
+#endif
 __device__ __forceinline__ unsigned long long *trace_stage(const DecodeParams &p, unsigned g, int k) {
 #ifdef QMC_DECODE_TRACE
     return (g_dtrace && blockIdx.x == 0 && g < (unsigned)kTrStages)
