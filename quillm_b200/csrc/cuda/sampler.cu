@@ -45,6 +45,7 @@ __device__ __forceinline__ uint32_t keyof(float v) { return __float_as_uint(v); 
 struct SelShared {
     int cnt[256];
     double mass[256];
+    uint32_t lo, hi;  // smallest / largest key in the set
     uint32_t prefix;
     int found;
     double rem;
@@ -60,18 +61,43 @@ template <typename InS>
 __device__ uint32_t select_key(const float *p, int n, InS in_s, int mode, double target, double *rest, bool *found,
                                SelShared &sh) {
     const int t = threadIdx.x;
-    if (t == 0) sh.prefix = 0, sh.found = 1, sh.rem = target;
+    if (t == 0) sh.lo = 0xffffffffu, sh.hi = 0u, sh.found = 1, sh.rem = target;
     __syncthreads();
+    // The bits that every key of S shares need no pass: the passes start at the highest bit where the
+    // smallest and largest keys differ.  (Nearly flat distributions share their top 10-20 bits; a pass
+    // over them would send every element to one bin, every update an atomic on the same address.)
+    {
+        uint32_t lo = 0xffffffffu, hi = 0u;
+        for (int i = t; i < n; i += kST) {
+            const float v = p[i];
+            if (in_s(i, v)) lo = min(lo, keyof(v)), hi = max(hi, keyof(v));
+        }
+        lo = __reduce_min_sync(0xffffffffu, lo);
+        hi = __reduce_max_sync(0xffffffffu, hi);
+        if ((t & 31) == 0) atomicMin(&sh.lo, lo), atomicMax(&sh.hi, hi);
+    }
+    __syncthreads();
+    const uint32_t lo = sh.lo, hi = sh.hi;
+    int bits = 0;  // low bits still to resolve (at least one pass: it checks the target against S's total)
     uint32_t pmask = 0;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int d = t; d < 256; d += kST) sh.cnt[d] = 0, sh.mass[d] = 0.0;
+    if (lo <= hi) {
+        bits = lo == hi ? 1 : 32 - __clz(lo ^ hi);
+        pmask = bits == 32 ? 0u : ~((1u << bits) - 1u);
+    } else if (t == 0) {
+        sh.found = 0;  // S is empty
+    }
+    if (t == 0) sh.prefix = lo & pmask;
+    __syncthreads();
+    while (bits > 0) {
+        const int w = bits < 8 ? bits : 8, shift = bits - w, nbin = 1 << w;
+        for (int d = t; d < nbin; d += kST) sh.cnt[d] = 0, sh.mass[d] = 0.0;
         __syncthreads();
         const uint32_t prefix = sh.prefix;
         for (int i = t; i < n; i += kST) {
             const float v = p[i];
             const uint32_t k = keyof(v);
             if ((k & pmask) == prefix && in_s(i, v)) {
-                const int d = (k >> shift) & 255;
+                const int d = (k >> shift) & (nbin - 1);
                 if (mode == 0) atomicAdd(&sh.cnt[d], 1);
                 else atomicAdd(&sh.mass[d], (double)v);
             }
@@ -80,20 +106,21 @@ __device__ uint32_t select_key(const float *p, int n, InS in_s, int mode, double
         if (t == 0 && sh.found) {
             double rem = sh.rem;
             int pick = -1;
-            for (int d = 255; d >= 0; d--) {
-                const double w = mode == 0 ? (double)sh.cnt[d] : sh.mass[d];
-                if (w > 0.0 && (mode == 2 ? rem < w : rem <= w)) {
+            for (int d = nbin - 1; d >= 0; d--) {
+                const double wd = mode == 0 ? (double)sh.cnt[d] : sh.mass[d];
+                if (wd > 0.0 && (mode == 2 ? rem < wd : rem <= wd)) {
                     pick = d;
                     break;
                 }
-                rem -= w;
+                rem -= wd;
             }
             if (pick < 0) sh.found = 0;
             else sh.prefix = prefix | ((uint32_t)pick << shift), sh.rem = rem;
         }
         __syncthreads();
         if (!sh.found) break;
-        pmask |= 255u << shift;
+        pmask |= (uint32_t)(nbin - 1) << shift;
+        bits = shift;
     }
     *rest = sh.rem;
     *found = sh.found != 0;
@@ -156,7 +183,7 @@ __device__ T block_sum(T v, T *red) {
     return s;
 }
 
-__global__ void __launch_bounds__(kST) sample_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kST, 1) sample_kernel(SampleArgs a) {
     __shared__ SelShared sh;
     __shared__ double redd[kST / 32];
     __shared__ int redi[kST / 32];
