@@ -42,9 +42,10 @@ __device__ __forceinline__ float rng_uniform(uint64_t *state) {
 __device__ __forceinline__ uint32_t keyof(float v) { return __float_as_uint(v); }
 
 // shared scratch of the selections
+constexpr int kDigit = 11, kBins = 1 << kDigit;  // key bits per selection pass, bins per pass
 struct SelShared {
-    int cnt[256];
-    double mass[256];
+    int cnt[kBins];
+    double mass[kBins];
     uint32_t lo, hi;  // smallest / largest key in the set
     uint32_t prefix;
     int found;
@@ -89,7 +90,7 @@ __device__ uint32_t select_key(const float *p, int n, InS in_s, int mode, double
     if (t == 0) sh.prefix = lo & pmask;
     __syncthreads();
     while (bits > 0) {
-        const int w = bits < 8 ? bits : 8, shift = bits - w, nbin = 1 << w;
+        const int w = bits < kDigit ? bits : kDigit, shift = bits - w, nbin = 1 << w;
         for (int d = t; d < nbin; d += kST) sh.cnt[d] = 0, sh.mass[d] = 0.0;
         __syncthreads();
         const uint32_t prefix = sh.prefix;
@@ -103,19 +104,36 @@ __device__ uint32_t select_key(const float *p, int n, InS in_s, int mode, double
             }
         }
         __syncthreads();
-        if (t == 0 && sh.found) {
-            double rem = sh.rem;
-            int pick = -1;
-            for (int d = nbin - 1; d >= 0; d--) {
-                const double wd = mode == 0 ? (double)sh.cnt[d] : sh.mass[d];
-                if (wd > 0.0 && (mode == 2 ? rem < wd : rem <= wd)) {
-                    pick = d;
-                    break;
-                }
-                rem -= wd;
+        // the bin where the descending cumulative weight reaches the target: warp 0, lane l summing bins
+        // nbin-1-l*c .. down (c = nbin/32), a warp scan of the lane sums, then the first lane whose range
+        // holds the target walks its bins
+        if (t < 32 && sh.found) {
+            const int c = nbin >= 32 ? nbin / 32 : 1, top = nbin - 1 - t * c;
+            double tot = 0.0;
+            if (top >= 0)
+                for (int e = 0; e < c; e++) tot += mode == 0 ? (double)sh.cnt[top - e] : sh.mass[top - e];
+            double incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (t >= o) incl += y;
             }
-            if (pick < 0) sh.found = 0;
-            else sh.prefix = prefix | ((uint32_t)pick << shift), sh.rem = rem;
+            const double rem = sh.rem - (incl - tot);  // what is left of the target when this range starts
+            const bool here = top >= 0 && tot > 0.0 && (mode == 2 ? rem < tot : rem <= tot);
+            const unsigned hit = __ballot_sync(0xffffffffu, here);
+            if (hit == 0) {
+                if (t == 0) sh.found = 0;
+            } else if (t == __ffs(hit) - 1) {
+                double r = rem;
+                int pick = top;
+                for (int e = 0; e < c; e++) {
+                    const double wd = mode == 0 ? (double)sh.cnt[top - e] : sh.mass[top - e];
+                    pick = top - e;
+                    if (wd > 0.0 && (mode == 2 ? r < wd : r <= wd)) break;
+                    r -= wd;
+                }
+                sh.prefix = prefix | ((uint32_t)pick << shift), sh.rem = r;
+            }
         }
         __syncthreads();
         if (!sh.found) break;
