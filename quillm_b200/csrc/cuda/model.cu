@@ -752,9 +752,10 @@ int prefill_proj_tc(qmc_model *m, int dt, const uint8_t *Ws, const float *A, int
     if (A) RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream, m->pf_adT, matmul_tc_scale_ld(T)));
     return launch_matmul_q_tc(dt, Ws, split_row_bytes(dt, K), m->pf_aq, m->pf_adT, C, C2, T, N, K, ctx()->err, m->stream);
 }
-// rmsnorm(x) * w straight into the activation blocks of the next tensor-core contraction
-int prefill_norm_quant(qmc_model *m, const float *w, int T) {
-    return launch_rmsnorm_quant_rows(m->pf_x, w, T, m->D, m->cfg.norm_eps, m->pf_aq, m->pf_ad, m->pf_adT,
+// x += add (when given), then rmsnorm(x) * w straight into the activation blocks of the next tensor-core
+// contraction
+int prefill_norm_quant(qmc_model *m, const float *add, const float *w, int T) {
+    return launch_rmsnorm_quant_rows(m->pf_x, add, w, T, m->D, m->cfg.norm_eps, m->pf_aq, m->pf_ad, m->pf_adT,
                                      matmul_tc_scale_ld(T), m->stream);
 }
 }  // namespace
@@ -780,8 +781,8 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     for (int l = 0; l < m->L; l++) {
         Layer &Ly = m->layers[l];
         void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
-        if (tc) {
-            RC(prefill_norm_quant(m, Ly.attn_norm, n));
+        if (tc) {  // the previous layer's w2 residual is added here, fused with the norm
+            RC(prefill_norm_quant(m, l > 0 ? m->pf_c : nullptr, Ly.attn_norm, n));
             RC(prefill_proj_tc(m, Ly.dt[QMC_T_WQ], Ly.sqkv, nullptr, n, NQKV, D, m->pf_qkv, nullptr));
         } else {
             RC(launch_rmsnorm_rows(m->pf_x, Ly.attn_norm, m->pf_xn, n, D, eps, s));
@@ -792,11 +793,11 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
                                vcl, m->kv16 != 0, m->pf_att, s));
         if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WO], Ly.swo, m->pf_att, n, D, Dq, m->pf_c, nullptr));
         else RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
-        RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
-        if (tc) {
-            RC(prefill_norm_quant(m, Ly.ffn_norm, n));
+        if (tc) {  // wo residual fused with the norm
+            RC(prefill_norm_quant(m, m->pf_c, Ly.ffn_norm, n));
             RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.s13, nullptr, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
         } else {
+            RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
             RC(launch_rmsnorm_rows(m->pf_x, Ly.ffn_norm, m->pf_xn, n, D, eps, s));
             RC(prefill_proj(m, Ly.dt[QMC_T_W1], Ly.w1, m->pf_xn, n, H, D, m->pf_h));
             RC(prefill_proj(m, Ly.dt[QMC_T_W3], Ly.w3, m->pf_xn, n, H, D, m->pf_h3));
@@ -808,7 +809,8 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
             RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
             RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
         }
-        RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
+        // w2 residual: on the tensor-core path the next layer's norm adds it, except after the last layer
+        if (!tc || l == m->L - 1) RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
     }
     // logits of the last token: the output GEMV with the final rmsnorm fused, as a decode step's
     GemvArgs g;

@@ -41,16 +41,21 @@ __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__
 // rmsnorm of one row per block followed by its Q8_0 quantization, without the normalised row in memory:
 // the same operations as rmsnorm_rows then quantize_act (inv from the double sum of squares, v = (x * inv)
 // * w rounded twice, per 32-element block the reference's quantizer), so the blocks are bit-identical
-__global__ void rmsnorm_quant_rows_kernel(const float *__restrict__ x, const float *__restrict__ w, int64_t n, float eps,
-                                          int8_t *__restrict__ qs, float *__restrict__ d, float *__restrict__ dT,
-                                          int64_t ldT) {
+// With `add`, the row first takes the residual add x += add (written back; src/model.c:179,186).
+__global__ void rmsnorm_quant_rows_kernel(float *__restrict__ x, const float *__restrict__ add, const float *__restrict__ w,
+                                          int64_t n, float eps, int8_t *__restrict__ qs, float *__restrict__ d,
+                                          float *__restrict__ dT, int64_t ldT) {
     __shared__ double red[32];
     __shared__ float inv_s;
     const int64_t row = blockIdx.x;
-    const float *xr = x + row * n;
+    float *xr = x + row * n;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     double ss = 0.0;
-    for (int64_t i = t; i < n; i += blockDim.x) ss = fma((double)xr[i], (double)xr[i], ss);
+    for (int64_t i = t; i < n; i += blockDim.x) {
+        float v = xr[i];
+        if (add) xr[i] = v = __fadd_rn(v, add[row * n + i]);
+        ss = fma((double)v, (double)v, ss);
+    }
     ss = warp_sum_d(ss);
     if (lane == 0) red[warp] = ss;
     __syncthreads();
@@ -268,9 +273,9 @@ int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, i
     return QMC_OK;
 }
 
-int launch_rmsnorm_quant_rows(const float *x, const float *w, int64_t T, int64_t n, float eps, int8_t *qs, float *d,
-                              float *dT, int64_t ldT, cudaStream_t s) {
-    rmsnorm_quant_rows_kernel<<<(unsigned)T, 256, 0, s>>>(x, w, n, eps, qs, d, dT, ldT);
+int launch_rmsnorm_quant_rows(float *x, const float *add, const float *w, int64_t T, int64_t n, float eps, int8_t *qs,
+                              float *d, float *dT, int64_t ldT, cudaStream_t s) {
+    rmsnorm_quant_rows_kernel<<<(unsigned)T, 256, 0, s>>>(x, add, w, n, eps, qs, d, dT, ldT);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }

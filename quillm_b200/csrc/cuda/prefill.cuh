@@ -11,9 +11,10 @@ int launch_embed_rows(int dtype, const void *table, int64_t cols, const int *tok
 // out[t] = rmsnorm(x[t]) * w, per row as src/ops.c:93-98
 int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, int64_t n, float eps, cudaStream_t s);
 // the Q8_0 blocks (qs [T][nb*32], scales d [T][nb] and, with dT, dT[b * ldT + t]) of rmsnorm(x[t]) * w: the
-// same bits as launch_rmsnorm_rows followed by launch_quantize_act, in one pass
-int launch_rmsnorm_quant_rows(const float *x, const float *w, int64_t T, int64_t n, float eps, int8_t *qs, float *d,
-                              float *dT, int64_t ldT, cudaStream_t s);
+// same bits as launch_rmsnorm_rows followed by launch_quantize_act, in one pass; with `add` (not null) the
+// residual x += add happens first and is written back (the same bits as launch_add before them)
+int launch_rmsnorm_quant_rows(float *x, const float *add, const float *w, int64_t T, int64_t n, float eps, int8_t *qs,
+                              float *d, float *dT, int64_t ldT, cudaStream_t s);
 // the Q8_0 blocks of silu(g[t]) * u[t] (the SwiGLU rows, same bits as launch_swiglu then launch_quantize_act)
 int launch_swiglu_quant_rows(const float *g, const float *u, int64_t T, int64_t n, int8_t *qs, float *d, float *dT,
                              int64_t ldT, cudaStream_t s);
