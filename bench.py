@@ -418,6 +418,9 @@ def gpu_arm(args, wl: dict) -> dict | None:
 
     per_gpu_bytes = np.mean([model.step_bytes(p) for p in range(pos0, pos0 + K)])
     launches, persistent = model.decode_info()
+    tp_gen = tp_logits = None
+    if d.world > 1:  # the tensor-parallel model's own greedy run, for the TP=1 comparison below
+        tp_gen, tp_logits = parity_run(model, prompt, cfg)
     hbm, tflops, src = peaks()
     step_time = sec / K
     achieved = per_gpu_bytes / step_time / 1e9
@@ -447,6 +450,12 @@ def gpu_arm(args, wl: dict) -> dict | None:
         "clocks": clk,
     }
     model.close()
+    if d.world > 1:
+        # every rank has released its shard; rank 0 alone decodes the same prompt with the whole model on
+        # its GPU (TP=1) while the others wait at the barrier
+        if d.rank == 0:
+            out["tp_parity"] = tp_parity(qb, wl, prompt, tp_gen, tp_logits)
+        d.barrier()
     if d.rank == 0 and d.world == 1 and not args.quick:
         out.update(kernel_sweeps(qb, torch, wl, hbm, tflops, src))
         out["long_context"] = long_context(qb, wl, st, e0, e1, hbm)
@@ -454,6 +463,34 @@ def gpu_arm(args, wl: dict) -> dict | None:
         out["cpu_baseline"] = cpu_baseline(args, wl)
     d.close()
     return out if d.rank == 0 else None
+
+
+TP_PARITY_TOKENS = 16
+
+
+def parity_run(model, prompt, cfg: dict):
+    """greedy tokens after the prompt (device-resident generation from position 0) and the logits one
+    step further, on every rank of a tensor-parallel model (collectives inside) or on one GPU"""
+    gen = [int(t) for t in model.generate(prompt, TP_PARITY_TOKENS)]
+    logits = np.zeros(cfg["vocab_size"], np.float32)
+    model.forward(gen[-1], len(prompt) + TP_PARITY_TOKENS - 1, logits)
+    return gen, logits
+
+
+def tp_parity(qb, wl: dict, prompt, tp_gen, tp_logits) -> dict:
+    """the tensor-parallel run's greedy tokens and final logits against the same model on one GPU (TP=1,
+    rank 0, after the shards are freed): identical tokens expected; logits within the reference's
+    same-weights tolerance (2e-2 relative, tests/test_model.c:50-53)"""
+    m = qb.Model(dict(wl["cfg"]))
+    m.synthesize(wl["dtype"], wl["seed"], STD)
+    gen, logits = parity_run(m, prompt, wl["cfg"])
+    m.close()
+    rel = float(np.abs(logits - tp_logits).max() / np.abs(logits).max())
+    first = next((i for i, (a, b) in enumerate(zip(gen, tp_gen)) if a != b), None)
+    return {"reference": "the same model on 1 GPU (TP=1)", "tokens": TP_PARITY_TOKENS,
+            "identical_tokens": gen == tp_gen, "first_differing_token": first,
+            "max_rel_logit_diff": rel, "logits_within_2e-2": rel < 2e-2,
+            "positions": [len(prompt), len(prompt) + TP_PARITY_TOKENS - 1]}
 
 
 def long_context(qb, wl: dict, st, e0, e1, hbm: float, steps: int = 64) -> list:
@@ -564,52 +601,87 @@ def ref_model(wl: dict, name: str, threads: int):
     return best[2], best[1]
 
 
-def cpu_baseline(args, wl: dict) -> dict:
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown CPU"
+
+
+def host_ram_bytes() -> int:
+    try:
+        return os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_PHYS_PAGES")
+    except (ValueError, OSError):
+        return 0
+
+
+def model_file_bytes(wl: dict) -> int:
+    c = wl["cfg"]
+    D, H, L, V = c["dim"], c["hidden_dim"], c["n_layers"], c["vocab_size"]
+    kv = D // c["n_heads"] * c["n_kv_heads"]
+    rb = lambda n: row_bytes(wl["dtype"], n)  # noqa: E731
+    return L * ((D + 2 * kv) * rb(D) + D * rb(D) + 2 * H * rb(D) + D * rb(H)) + 2 * V * rb(D)
+
+
+def ref_decode(wl: dict, name: str, warmup: int, steps: int, time_cap: float | None = None):
+    """the reference's CPU decode as its own loop runs it (src/main.c:127-146): the whole prompt one
+    token at a time (untimed), `warmup` greedy steps, then up to `steps` timed greedy steps (fewer when
+    time_cap seconds run out).  Returns (steps timed, seconds, ISA name, threads, first timed position)."""
     from oracle import oracle as O
 
     threads = os.cpu_count() or 1
-    m, isa = ref_model(wl, args.workload, threads)
-    prompt = prompt_ids(wl)
-    npre = min(4, len(prompt))
-    for p in range(npre):
-        lg = m.forward(int(prompt[p]), p)
-    tok = int(np.argmax(lg))
-    n, t0 = 0, time.perf_counter()
-    while n < 64 and (time.perf_counter() - t0 < 10.0 or n < 3):
-        tok = int(np.argmax(m.forward(tok, npre + n)))
-        n += 1
-    sec = time.perf_counter() - t0
-    m.close()
-    names = {O.ISA_SCALAR: "scalar", O.ISA_AVX2: "avx2", O.ISA_AVX512: "avx512"}
-    return {"value": n / sec, "unit": "tok/s", "cores": threads, "kind": "reference",
-            "sample": f"reference qm_model_forward ({names[isa]}, {threads} threads), {args.workload}: "
-                      f"{npre} prompt tokens then {n} greedy decode tokens timed"}
-
-
-def reference_arm(args, wl: dict) -> dict | None:
-    rank = int(os.environ.get("RANK", 0))
-    if rank != 0:
-        return None
-    from oracle import oracle as O
-
-    threads = os.cpu_count() or 1
-    m, isa = ref_model(wl, args.workload, threads)
+    m, isa = ref_model(wl, name, threads)
     prompt = prompt_ids(wl)
     lg = None
     for p, t in enumerate(prompt):
         lg = m.forward(int(t), p)
     tok = int(np.argmax(lg))
     pos = len(prompt)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         tok = int(np.argmax(m.forward(tok, pos)))
         pos += 1
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
+    first, n, t0 = pos, 0, time.perf_counter()
+    while n < steps and (time_cap is None or n < 3 or time.perf_counter() - t0 < time_cap):
         tok = int(np.argmax(m.forward(tok, pos)))
         pos += 1
+        n += 1
     sec = time.perf_counter() - t0
     m.close()
     names = {O.ISA_SCALAR: "scalar", O.ISA_AVX2: "avx2", O.ISA_AVX512: "avx512"}
+    return n, sec, names[isa], threads, first
+
+
+def ram_refusal(wl: dict) -> str | None:
+    need, have = model_file_bytes(wl), host_ram_bytes()
+    if have and need > 0.8 * have:
+        return f"not run (host RAM): the {need / 1e9:.0f} GB model file does not fit in {have / 1e9:.0f} GB of host memory"
+    return None
+
+
+def cpu_baseline(args, wl: dict) -> dict:
+    why = ram_refusal(wl)
+    if why:
+        return {"value": None, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "reference", "sample": why}
+    n, sec, isa, threads, first = ref_decode(wl, args.workload, args.warmup, args.steps, time_cap=10.0)
+    return {"value": n / sec, "unit": "tok/s", "cores": threads, "kind": "reference", "cpu": cpu_model(),
+            "sample": f"reference qm_model_forward ({isa}, {threads} threads on {cpu_model()}), {args.workload}: "
+                      f"{wl['prompt']} prompt tokens and {args.warmup} warm-up steps untimed, then {n} greedy "
+                      f"decode steps timed at positions {first}-{first + n - 1} (the reference arm's)"}
+
+
+def reference_arm(args, wl: dict) -> dict | None:
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return None
+    why = ram_refusal(wl)
+    if why:
+        return {"impl": "reference", "unavailable": why}
+    n, sec, isa, threads, first = ref_decode(wl, args.workload, args.warmup, args.steps)
+    prompt = prompt_ids(wl)
+    pos = first + n
     v = args.steps / sec
     c = wl["cfg"]
     return {"metric": METRIC, "impl": "reference", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
@@ -619,8 +691,8 @@ def reference_arm(args, wl: dict) -> dict | None:
             "config": {"workload": f"{args.workload}_decode", "model": wl["model"], "global_batch": 1,
                        "seq_len": c["max_seq"], "prompt_tokens": len(prompt),
                        "decode_positions": [len(prompt) + args.warmup, pos - 1], "parallelism": "cpu"},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference",
-                             "sample": f"reference qm_model_forward ({names[isa]}, {threads} threads): "
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference", "cpu": cpu_model(),
+                             "sample": f"reference qm_model_forward ({isa}, {threads} threads on {cpu_model()}): "
                                        f"{len(prompt)} prompt tokens untimed, {args.warmup} warm-up and "
                                        f"{args.steps} timed greedy decode steps"},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

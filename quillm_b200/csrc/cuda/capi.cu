@@ -1,6 +1,7 @@
 // C-ABI entry points of libquillm_cuda (include/quillm_cuda.h): error state, per-device context and the
 // operator-level calls.  Model-level calls live in model.cu.
 #include <math.h>
+#include <stdint.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -363,7 +364,11 @@ int qmc_matmul_nt_q_noalloc(int dtype, const void *W, const float *A, float *C, 
     if (dtype == QMC_F32) return launch_gemm_f32(A, (const float *)W, C, T, N, K, s);
     if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "matmul_nt_q_noalloc: bad dtype %d", dtype);
     const int64_t nb = nblocks(K);
-    const size_t qbytes = (size_t)(T * nb * 32 + 255) / 256 * 256, need = qbytes + (size_t)T * nb * 4;
+    // T * nb * 36 must fit the array; compare by division first, so a huge T or K cannot wrap the
+    // products below into a small value that passes
+    const bool too_big = T > (int64_t)(kNoAllocScratchBytes / 36) / nb;
+    const size_t qbytes = too_big ? 0 : (size_t)(T * nb * 32 + 255) / 256 * 256;
+    const size_t need = too_big ? SIZE_MAX : qbytes + (size_t)T * nb * 4;
     if (need > kNoAllocScratchBytes)
         return set_error(QMC_EINVAL,
                          "matmul_nt_q_noalloc: T=%lld x K=%lld needs %zu bytes of scratch, above the fixed %zu "

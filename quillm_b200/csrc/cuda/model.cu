@@ -36,7 +36,8 @@ struct Layer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     uint8_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w3 = nullptr, *w2 = nullptr;
     uint8_t *sqkv = nullptr, *swo = nullptr, *s13 = nullptr, *sw2 = nullptr;  // split-row copies (persistent path)
-    int dt[12];  // dtype per uploaded kind (indices QMC_T_*), -1 = missing
+    int dt[12];          // dtype per uploaded kind (indices QMC_T_*), -1 = missing
+    unsigned dirty = 0;  // kinds (bit QMC_T_*) uploaded since the split-row copies were last refilled
 };
 }  // namespace
 
@@ -66,7 +67,7 @@ struct qmc_model {
     cudaGraphExec_t graph = nullptr;
     bool have_tok = false, have_norm = false, have_out = false;
     // persistent decode path (tp 1, quantized matrices): split-row weights, phase list, barrier state
-    bool mega = false, mega_checked = false, repacked = false;
+    bool mega = false, mega_checked = false, repacked = false, out_dirty = true;
     DecodePlan plan;
     std::vector<DecodePhase> phases;
     DecodePhase *d_phases = nullptr;
@@ -97,6 +98,20 @@ int dalloc(qmc_model *m, void **p, size_t bytes) {
     cudaError_t e = cudaMalloc(p, bytes + 256);  // slack: 16-byte line reads past a tensor's end stay inside
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(model)");
     m->allocs.push_back(*p);
+    return QMC_OK;
+}
+
+// release one model buffer (no kernel may still use it: the caller synchronised the stream)
+template <typename T>
+int dfree(qmc_model *m, T **p) {
+    if (!*p) return QMC_OK;
+    for (size_t i = 0; i < m->allocs.size(); i++)
+        if (m->allocs[i] == (void *)*p) {
+            m->allocs.erase(m->allocs.begin() + (long)i);
+            break;
+        }
+    QMC_CUDA(cudaFree((void *)*p));
+    *p = nullptr;
     return QMC_OK;
 }
 
@@ -198,8 +213,8 @@ int dest_of(qmc_model *m, int kind, int layer, int dt, uint8_t **dst) {
 void mark(qmc_model *m, int kind, int layer, int dt) {
     if (kind == QMC_T_TOK_EMBD) m->have_tok = true;
     else if (kind == QMC_T_NORM) m->have_norm = true;
-    else if (kind == QMC_T_OUTPUT) m->have_out = true;
-    else m->layers[layer].dt[kind] = dt;
+    else if (kind == QMC_T_OUTPUT) m->have_out = true, m->out_dirty = true;
+    else m->layers[layer].dt[kind] = dt, m->layers[layer].dirty |= 1u << kind;
 }
 
 bool complete(const qmc_model *m) {
@@ -240,27 +255,45 @@ bool decode_eligible(qmc_model *m, DevCtx *c) {
     return plan_decode(umax, nbmax, m->hd, m->NH / m->NKV, c->max_smem_optin, &m->plan);
 }
 
-// split-row copies of every matrix (allocated once, refilled after any upload); FFN rows interleaved
-// w1[0], w3[0], w1[1], ... so one copy streams both rows of a SwiGLU unit
+// split-row copies of every matrix (allocated once); FFN rows interleaved w1[0], w3[0], w1[1], ... so one
+// copy streams both rows of a SwiGLU unit.  Only the kinds uploaded since the last refill are repacked,
+// layer by layer, and each layer's file-layout copies are released right after: the persistent path
+// reads only the split-row copies (and prefill the same), so the model holds its weights once.  A later
+// upload of one tensor allocates its file-layout buffer again, and only its rows are repacked.  The
+// output matrix keeps its file-layout copy too (the batched prompt forward's final GEMV reads it).
 int repack_weights(qmc_model *m) {
     cudaStream_t s = m->stream;
     for (Layer &l : m->layers) {
         const int dq = l.dt[QMC_T_WQ], dw = l.dt[QMC_T_WO], d1 = l.dt[QMC_T_W1], d2 = l.dt[QMC_T_W2];
         const int64_t rq = split_row_bytes(dq, m->D), ro = split_row_bytes(dw, m->Dl), r1 = split_row_bytes(d1, m->D),
                       r2 = split_row_bytes(d2, m->Hl);
-        const int64_t nq = m->Dl + 2 * m->KVl;
+        const int64_t nq = m->Dl + 2 * m->KVl, aq = rbytes(dq, m->D);
         if (!l.sqkv && (dalloc(m, (void **)&l.sqkv, (size_t)(nq * rq)) || dalloc(m, (void **)&l.swo, (size_t)(m->D * ro)) ||
                         dalloc(m, (void **)&l.s13, (size_t)(2 * m->Hl * r1)) || dalloc(m, (void **)&l.sw2, (size_t)(m->D * r2))))
             return QMC_ENOMEM;
-        RC(launch_repack_split(dq, l.wqkv, nq, m->D, l.sqkv, rq, s));
-        RC(launch_repack_split(dw, l.wo, m->D, m->Dl, l.swo, ro, s));
-        RC(launch_repack_split(d1, l.w1, m->Hl, m->D, l.s13, 2 * r1, s));
-        RC(launch_repack_split(d1, l.w3, m->Hl, m->D, l.s13 + r1, 2 * r1, s));
-        RC(launch_repack_split(d2, l.w2, m->D, m->Hl, l.sw2, r2, s));
+        const unsigned d = l.dirty;
+        if (!d) continue;
+        // wq | wk | wv row ranges of the stacked matrix
+        const int64_t q0[3] = {0, m->Dl, m->Dl + m->KVl}, qn[3] = {m->Dl, m->KVl, m->KVl};
+        const int qk[3] = {QMC_T_WQ, QMC_T_WK, QMC_T_WV};
+        for (int j = 0; j < 3; j++)
+            if (d & (1u << qk[j])) RC(launch_repack_split(dq, l.wqkv + q0[j] * aq, qn[j], m->D, l.sqkv + q0[j] * rq, rq, s));
+        if (d & (1u << QMC_T_WO)) RC(launch_repack_split(dw, l.wo, m->D, m->Dl, l.swo, ro, s));
+        if (d & (1u << QMC_T_W1)) RC(launch_repack_split(d1, l.w1, m->Hl, m->D, l.s13, 2 * r1, s));
+        if (d & (1u << QMC_T_W3)) RC(launch_repack_split(d1, l.w3, m->Hl, m->D, l.s13 + r1, 2 * r1, s));
+        if (d & (1u << QMC_T_W2)) RC(launch_repack_split(d2, l.w2, m->D, m->Hl, l.sw2, r2, s));
+        QMC_CUDA(cudaStreamSynchronize(s));
+        RC(dfree(m, &l.wqkv));
+        RC(dfree(m, &l.wo));
+        RC(dfree(m, &l.w1));
+        RC(dfree(m, &l.w3));
+        RC(dfree(m, &l.w2));
+        l.dirty = 0;
     }
     const int64_t rout = split_row_bytes(m->dt_out, m->D);
     if (!m->sout && dalloc(m, (void **)&m->sout, (size_t)(m->Vl * rout))) return QMC_ENOMEM;
-    RC(launch_repack_split(m->dt_out, m->out, m->Vl, m->D, m->sout, rout, s));
+    if (m->out_dirty) RC(launch_repack_split(m->dt_out, m->out, m->Vl, m->D, m->sout, rout, s));
+    m->out_dirty = false;
     QMC_CUDA(cudaStreamSynchronize(s));
     m->repacked = true;
     return QMC_OK;

@@ -124,13 +124,27 @@ __device__ uint32_t select_key(const float *p, int n, InS in_s, int mode, double
             if (hit == 0) {
                 if (t == 0) sh.found = 0;
             } else if (t == __ffs(hit) - 1) {
-                double r = rem;
-                int pick = top;
-                for (int e = 0; e < c; e++) {
+                // the walk subtracts bin by bin, which need not reproduce `tot`'s rounding: if it runs
+                // off the range's end, the pick stays the last bin that holds weight (with what was
+                // left of the target clamped into it), never an empty bin
+                double r = rem, last_w = 0.0;
+                int pick = top, last = top;
+                bool hit_bin = false;
+                for (int e = 0; e < c && !hit_bin; e++) {
                     const double wd = mode == 0 ? (double)sh.cnt[top - e] : sh.mass[top - e];
-                    pick = top - e;
-                    if (wd > 0.0 && (mode == 2 ? r < wd : r <= wd)) break;
-                    r -= wd;
+                    if (wd > 0.0) {
+                        if (mode == 2 ? r < wd : r <= wd) {
+                            pick = top - e;
+                            hit_bin = true;
+                        } else {
+                            last = top - e, last_w = wd;
+                            r -= wd;
+                        }
+                    }
+                }
+                if (!hit_bin) {  // ran off the end: the last bin with weight, the target at its far edge
+                    pick = last;
+                    r = mode == 2 ? nextafter(last_w, 0.0) : last_w;
                 }
                 sh.prefix = prefix | ((uint32_t)pick << shift), sh.rem = r;
             }
@@ -363,6 +377,17 @@ struct qmc_sampler {
     int32_t *h_out = nullptr; // pinned
 };
 
+namespace {
+// make the sampler's device current: its buffers live there, and a kernel launched on another device
+// would read and write them through peer addresses (or fault without peer access)
+int sampler_device(const qmc_sampler *s) {
+    int d = -1;
+    QMC_CUDA(cudaGetDevice(&d));
+    if (d != s->dev) QMC_CUDA(cudaSetDevice(s->dev));
+    return QMC_OK;
+}
+}  // namespace
+
 extern "C" {
 
 int qmc_sampler_create(int32_t n_vocab, float temperature, int32_t top_k, float top_p, uint64_t seed,
@@ -370,8 +395,10 @@ int qmc_sampler_create(int32_t n_vocab, float temperature, int32_t top_k, float 
     using namespace qmc;
     if (!out || n_vocab < 1) return set_error(QMC_EINVAL, "sampler_create: bad arguments");
     *out = nullptr;
+    int dev = -1;
+    QMC_CUDA(cudaGetDevice(&dev));
     qmc_sampler *s = new qmc_sampler();
-    QMC_CUDA(cudaGetDevice(&s->dev));
+    s->dev = dev;
     s->n = n_vocab;
     // the reference's normalisation of the settings (src/sampler.c:8-11)
     s->temperature = temperature < 0 ? 0 : temperature;
@@ -394,6 +421,7 @@ int qmc_sampler_create(int32_t n_vocab, float temperature, int32_t top_k, float 
 int qmc_sampler_enqueue(qmc_sampler *s, const float *dev_logits, int32_t *dev_token, void *stream) {
     using namespace qmc;
     if (!s || !dev_logits || !dev_token) return set_error(QMC_EINVAL, "sampler_enqueue: null argument");
+    if (const int rc = sampler_device(s)) return rc;
     return launch_sample(dev_logits, s->n, s->temperature, s->top_k, s->top_p, s->rng, s->p, dev_token,
                          pick_stream(stream));
 }
@@ -401,6 +429,7 @@ int qmc_sampler_enqueue(qmc_sampler *s, const float *dev_logits, int32_t *dev_to
 int qmc_sampler_sample(qmc_sampler *s, const float *dev_logits, int32_t *token) {
     using namespace qmc;
     if (!s || !dev_logits || !token) return set_error(QMC_EINVAL, "sampler_sample: null argument");
+    if (const int rc = sampler_device(s)) return rc;
     cudaStream_t st = pick_stream(nullptr);
     const int rc = launch_sample(dev_logits, s->n, s->temperature, s->top_k, s->top_p, s->rng, s->p, s->out, st);
     if (rc) return rc;
@@ -413,6 +442,7 @@ int qmc_sampler_sample(qmc_sampler *s, const float *dev_logits, int32_t *token) 
 int qmc_sampler_rng(qmc_sampler *s, uint64_t *state) {
     using namespace qmc;
     if (!s || !state) return set_error(QMC_EINVAL, "sampler_rng: null argument");
+    if (const int rc = sampler_device(s)) return rc;
     QMC_CUDA(cudaDeviceSynchronize());
     QMC_CUDA(cudaMemcpy(state, s->rng, 8, cudaMemcpyDeviceToHost));
     return QMC_OK;
@@ -420,6 +450,7 @@ int qmc_sampler_rng(qmc_sampler *s, uint64_t *state) {
 
 int qmc_sampler_free(qmc_sampler *s) {
     if (!s) return QMC_OK;
+    cudaSetDevice(s->dev);
     cudaFree(s->rng);
     cudaFree(s->p);
     cudaFree(s->out);

@@ -50,13 +50,15 @@ def test_two_gloo_ranks_share_id_and_reduce_max(tmp_path):
 
 
 @pytest.mark.gpu
-def test_tp_matches_single_gpu(tmp_path):
-    """tensor-parallel decode over 2 GPUs (NCCL, one process per GPU) gives the single-GPU tokens and
-    logits within the reference's tolerance (tests/test_model.c:50-53, 2e-2 relative)"""
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_matches_single_gpu(tmp_path, world):
+    """tensor-parallel decode over 2, 4 or 8 GPUs (NCCL, one process per GPU; GQA group 2, so at 8 ranks
+    each holds one KV head and its two query heads) gives the single-GPU tokens and logits within the
+    reference's tolerance (tests/test_model.c:50-53, 2e-2 relative)"""
     import torch
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     script = tmp_path / "tp.py"
     script.write_text(f"""
 import os, sys, numpy as np
@@ -67,7 +69,7 @@ rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
 torch.cuda.set_device(rank)
 qb.check(qb.cuda().qmc_set_device(rank))
 dist.init_process_group("gloo")
-cfg = dict(dim=256, hidden_dim=704, n_layers=3, n_heads=8, n_kv_heads=4, vocab_size=3000, max_seq=64)
+cfg = dict(dim=512, hidden_dim=1024, n_layers=3, n_heads=16, n_kv_heads=8, vocab_size=3000, max_seq=64)
 buf = C.create_string_buffer(128)
 if rank == 0:
     qb.check(qb.cuda().qmc_nccl_unique_id(buf))
@@ -96,10 +98,10 @@ dist.destroy_process_group()
 """)
     port = _free_port()
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(port), str(script)]
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(port), str(script)]
     r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     assert r.returncode == 0, r.stderr[-3000:]
     same, rel = open(tmp_path / "res.txt").read().split()
-    print(f"tp2 vs tp1: identical greedy tokens {same}, max rel logit diff {float(rel):.2e}")
+    print(f"tp{world} vs tp1: identical greedy tokens {same}, max rel logit diff {float(rel):.2e}")
     assert same == "True"
     assert float(rel) < 2e-2

@@ -58,7 +58,11 @@ def test_golden_models(cuda_dev, name, tol_deq, tol_fp):
     # same weights, same activation quantization: the reference's own C forward
     orc = O.OracleModel(path)
     want = np.stack([orc.forward(t, p) for p, t in enumerate(toks)])
-    assert np.abs(got - want).max() / np.abs(want).max() < tol_deq
+    e_c = np.abs(got - want).max() / np.abs(want).max()
+    print(f"{name}: rel err vs numpy float64 {e:.3e} (fp32 weights {efp:.3e}), vs the C forward {e_c:.3e}")
+    # both sides quantize the activations bit-exactly, so only the accumulation order differs: far inside
+    # the reference's own tolerance (observed at most ~1e-7 on these models)
+    assert e_c < 1e-5, e_c
     # run-to-run determinism (bitwise) and error returns
     again = np.stack([m.forward(t, p) for p, t in enumerate(toks)])
     assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
@@ -134,7 +138,7 @@ def test_stories15m_q8_greedy_parity(cuda_dev, tmp_path):
     m = DropIn(path)
     max_rel, ties = greedy_parity(m.forward, m.generate, rm, prompt, 64)
     print(f"stories15M q8: max rel logit err vs reference scalar {max_rel:.3e}, tie steps {ties}")
-    assert max_rel < 2e-2
+    assert max_rel < 1e-4
     m.close()
 
 

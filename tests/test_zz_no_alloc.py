@@ -54,3 +54,7 @@ def test_noalloc_rejects_oversized_scratch(cuda_dev):
     # T * ceil(K/32) * 36 = 4096 * 128 * 36 bytes = 18 MiB > 8 MiB: refused before touching any pointer
     rc = lib.qmc_matmul_nt_q_noalloc(O.Q8_0, buf.data_ptr(), buf.data_ptr(), buf.data_ptr(), 4096, 8, 4096, None)
     assert rc == -1 and b"fixed" in qb.cuda().qmc_last_error()
+    # sizes whose byte count would wrap a 64-bit product (T * 36 > 2^64) are refused the same way
+    for T, K in ((2**62 + 1, 32), (2**40, 2**40)):
+        rc = lib.qmc_matmul_nt_q_noalloc(O.Q8_0, buf.data_ptr(), buf.data_ptr(), buf.data_ptr(), T, 8, K, None)
+        assert rc == -1 and b"fixed" in qb.cuda().qmc_last_error(), (T, K)
