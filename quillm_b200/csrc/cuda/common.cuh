@@ -166,6 +166,26 @@ __device__ __forceinline__ bool counter_wait(const unsigned *ctr, unsigned targe
         if (clock64() - t0 > kWaitCycles) return false;
     return true;
 }
+// L2 policy for data read once (streamed weights): evicted first, so activations, partials and the KV
+// cache stay in L2 while gigabytes of weights pass through it
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// global -> shared bulk copy completing on `bar`, with an L2 cache policy; dst, src 16-byte aligned,
+// bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+// bring the 128-byte line holding p into L2, kept there in preference to evict-first lines
+__device__ __forceinline__ void prefetch_l2_keep(const void *p) {
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
 // global -> shared bulk copy completing on `bar`; dst, src 16-byte aligned, bytes % 16 == 0
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

@@ -207,6 +207,7 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
     };
     settle();
     unsigned g_last = 0, nissued = 0;  // this lane's last issued stage and its count (for the drain)
+    const uint64_t pol = l2_evict_first_policy();  // each weight byte is read once per step
     const long long t0 = clock64();
     while (true) {
         bool done = i >= p.nph, issued = false;
@@ -221,7 +222,7 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
                 if (k + NG >= nst) DTRACE_MAX(i, kTrProdLast, gtime());
                 if (unsigned long long *q_ = trace_stage(p, g, 0)) *q_ = gtime();
                 mbar_arrive_tx(&full[s], bytes);
-                bulk_g2s(sm + (size_t)s * p.slot_bytes, q.W + ua * ubytes, bytes, &full[s]);
+                bulk_g2s_hint(sm + (size_t)s * p.slot_bytes, q.W + ua * ubytes, bytes, &full[s], pol);
                 g_last = g, nissued++;
                 k += NG;
                 settle();
@@ -789,6 +790,25 @@ __device__ __forceinline__ int att_dim(int lane, int w) {
     return F16 ? 64 * (w >> 1) + 2 * lane + (w & 1) : lane + 32 * w;
 }
 
+// The K and V rows this CTA's attention unit reads in the coming phase, brought into L2 (kept there in
+// preference to the streamed weights) once the CTA's QKV work is done: their loads after the grid
+// barrier then hit L2 instead of waiting on HBM.  Rows of earlier positions are fixed for the step; the
+// row of `pos`, written during the QKV phase, is coherent in L2 either way (all cache reads are .cg).
+template <typename KT>
+__device__ void attn_prefetch(const DecodeParams &p, const DecodePhase &ph, int pos) {
+    const int npos = pos + 1, nseg = attn_segments(p, pos);
+    if ((int)blockIdx.x >= p.nkv * p.gsplit * nseg) return;
+    const int unit = (int)blockIdx.x / nseg, seg = (int)blockIdx.x % nseg, kvh = unit / p.gsplit;
+    const int chunk = (npos + nseg - 1) / nseg, t0 = seg * chunk, t1 = min(npos, t0 + chunk);
+    const int rowb = p.hd * (int)sizeof(KT), lines = (rowb + 127) / 128 + 1;  // +1: the row's last byte
+    const int total = max(0, t1 - t0) * 2 * lines;
+    for (int e = threadIdx.x; e < total; e += NCT) {
+        const int tt = t0 + e / (2 * lines), r = e % (2 * lines), kv = r / lines, ln = r % lines;
+        const uint8_t *row = (const uint8_t *)((const KT *)(kv ? ph.vc : ph.kc) + (int64_t)tt * p.KVl + (int64_t)kvh * p.hd);
+        prefetch_l2_keep(row + min(ln * 128, rowb - 1));
+    }
+}
+
 template <typename KT>  // cache element: float or __half
 __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int pos) {
     constexpr bool F16 = std::is_same<KT, __half>::value;
@@ -914,60 +934,47 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
             }
         }
     }
-    // merge the warps: tree over shared memory (the activation area is free during attention)
-    float *scr = (float *)(sm + p.off_xq);
-    for (int n = NCW; n > 1;) {
-        const int h = (n + 1) / 2;  // warps [h, n) hand their state to warps [0, n - h)
-        if (warp >= h && warp < n) {
-#pragma unroll
-            for (int g = 0; g < GMAX; g++) {
-                if (g < G) {
-                    float *dst = scr + ((warp - h) * GMAX + g) * stride;
-                    if (lane == 0) dst[0] = m[g], dst[1] = l[g];
-#pragma unroll
-                    for (int w = 0; w < MAXW; w++) {
-                        const int d = att_dim<F16>(lane, w);
-                        if (d < hd) dst[2 + d] = o[g][w];
-                    }
-                }
-            }
-        }
-        named_sync(kBarConsumers, NCT);
-        if (warp < n - h) {
-#pragma unroll
-            for (int g = 0; g < GMAX; g++) {
-                if (g < G) {
-                    const float *src = scr + (warp * GMAX + g) * stride;
-                    const float m2 = src[0], l2 = src[1], M = fmaxf(m[g], m2);
-                    const float c1 = l[g] > 0.0f ? expf(m[g] - M) : 0.0f, c2 = l2 > 0.0f ? expf(m2 - M) : 0.0f;
-                    l[g] = l[g] * c1 + l2 * c2;
-#pragma unroll
-                    for (int w = 0; w < MAXW; w++) {
-                        const int d = att_dim<F16>(lane, w);
-                        if (d < hd) o[g][w] = o[g][w] * c1 + src[2 + d] * c2;
-                    }
-                    m[g] = M;
-                }
-            }
-        }
-        named_sync(kBarConsumers, NCT);
-        n = h;
-    }
-    if (!active || warp != 0) return;
-    // this segment's (max, sum, acc) per query head -> global; the wo phase's prologue merges the
-    // segments of each head while it quantizes the attention output (src/model.c:141-153)
-    float *part = p.apart + ((int64_t)unit * p.maxseg + seg) * GMAX * ps;
+    // merge the warps in one pass (the activation area is free during attention): every warp's (max, sum)
+    // and acc per query head go to shared memory, then each consumer thread merges one (head, dimension)
+    // over the NCW warps in warp order -- one CTA barrier instead of a tree of them -- and writes this
+    // segment's (max, sum, acc) partial to global memory; the wo phase's prologue merges the segments of
+    // each head while it quantizes the attention output (src/model.c:141-153)
+    float *scr = (float *)(sm + p.off_xq);  // [NCW][G][hd + 2]
 #pragma unroll
     for (int g = 0; g < GMAX; g++) {
         if (g < G) {
-            float *dst = part + g * ps;
-            if (lane == 0) __stcg(dst, m[g]), __stcg(dst + 1, l[g]);
+            float *dst = scr + (warp * G + g) * stride;
+            if (lane == 0) dst[0] = m[g], dst[1] = l[g];
 #pragma unroll
             for (int w = 0; w < MAXW; w++) {
                 const int d = att_dim<F16>(lane, w);
-                if (d < hd) __stcg(dst + kPartHead + d, o[g][w]);
+                if (d < hd) dst[2 + d] = o[g][w];
             }
         }
+    }
+    named_sync(kBarConsumers, NCT);
+    if (!active) return;  // the grid barrier that follows starts with a CTA barrier: the scratch stays
+                          // untouched until every thread has read it
+    float *part = p.apart + ((int64_t)unit * p.maxseg + seg) * GMAX * ps;
+    for (int e = t; e < G * (hd + 1); e += NCT) {  // (head, dimension) pairs; dimension hd: (max, sum)
+        const int g = e / (hd + 1), d = e % (hd + 1);
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NCW; w++) {
+            const float *src = scr + (w * G + g) * stride;
+            if (src[1] > 0.0f) M = fmaxf(M, src[0]);
+        }
+        float den = 0.0f, acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NCW; w++) {
+            const float *src = scr + (w * G + g) * stride;
+            const float lw = src[1], c = lw > 0.0f ? expf(src[0] - M) : 0.0f;
+            den = fmaf(c, lw, den);
+            if (d < hd) acc = fmaf(c, src[2 + d], acc);
+        }
+        float *dst = part + g * ps;
+        if (d == hd) __stcg(dst, M), __stcg(dst + 1, den);
+        else __stcg(dst + kPartHead + d, acc);
     }
 }
 
@@ -1049,6 +1056,10 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
         if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
         else run_matvec<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
         if (ph.kind == PH_OUT) logits_argmax(p, sm, best);
+        if (ph.kind == PH_QKV) {  // the attention phase that follows reads this layer's cache
+            if constexpr (KV16) attn_prefetch<__half>(p, ph, pos);
+            else attn_prefetch<float>(p, ph, pos);
+        }
     }
 }
 
@@ -1092,8 +1103,8 @@ bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t s
     if (hd > 32 * MAXW) return false;
     auto r128 = [](int64_t b) { return (b + 127) / 128 * 128; };
     const int64_t act = r128((int64_t)nb_max * 32) + r128((int64_t)nb_max * 8);
-    const int64_t tree = r128((int64_t)(NCW / 2) * GMAX * (hd + 2) * 4);  // [warps handing over][GMAX][hd + 2]
-    (void)group;
+    // attention merge scratch: every warp's (max, sum, acc) per query head of a unit
+    const int64_t tree = r128((int64_t)NCW * std::min(std::max(group, 1), GMAX) * (hd + 2) * 4);
     const int64_t scratch = std::max(act, tree);
     for (int ns : {3 * NG, 2 * NG, NG}) {  // slots: a multiple of NG, so every slot belongs to one group
         const int64_t bars = r128((int64_t)ns * 2 * 8);  // full[ns], empty[ns]

@@ -1,9 +1,26 @@
-/* .qlm loader: bounds-checked parser over a read-only private mapping (format in include/qlm_file.h).
- * Same acceptance rules as the reference loader (src/qlm_file.c:73-150): every count, name, dtype,
- * shape, offset and size is checked against the buffer before use; a failure frees everything and
- * returns -1 with a message. */
+/* .qlm loader over a read-only private mapping (format in include/qlm_file.h).
+ *
+ * The header is walked with one explicit byte position and one bounds predicate (`fits`): nothing is
+ * read before it is known to lie inside the buffer.  Each section has its own small parser that reports
+ * success or failure; qlm_parse turns a failure into a message naming the section, the entry index and
+ * the byte position, frees what it allocated and returns -1.
+ *
+ * What a file must satisfy to load (the reference loader's acceptance rules, src/qlm_file.c:73-150;
+ * tests/test_loader.py checks acceptance and the parsed result against the compiled reference on
+ * thousands of mutated headers):
+ *   prelude  "QLMF", version 1, at most QLM_MAX_KV key/value entries and QLM_MAX_TENSORS tensors, and
+ *            a data offset that is a multiple of QM_ALIGN and not past the end of the file;
+ *   entries  a key of 1..63 bytes with no NUL; a value of type u32 or f32 (4 bytes), string (u32 length
+ *            and that many bytes) or u32 array (u32 count and 4 bytes per element);
+ *   tensors  a name of 1..63 bytes with no NUL; a known dtype; 1..4 dimensions, each in [1, 2^40],
+ *            whose product is at most 2^40; an offset that is a multiple of QM_ALIGN; the tensor's bytes
+ *            inside the data region;
+ *   and the header ends at or before the data offset.
+ * The messages "bad magic" and "unsupported version N" are the ones callers of the reference see and
+ * test for; the others are this loader's own. */
 #include "qlm_file.h"
 
+#include <errno.h>
 #include <fcntl.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -13,37 +30,52 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#define QLM_PRELUDE_BYTES 24u            /* magic, version, n_kv, n_tensors, data offset */
+#define QLM_MAX_ELEMS ((uint64_t)1 << 40) /* per dimension and per tensor */
+
 typedef struct {
-    const uint8_t *buf;
-    size_t size, at;
-    int broken; /* sticky: set by the first out-of-range read */
-} cursor;
+    const uint8_t *base;
+    size_t size; /* bytes in the buffer */
+    size_t pos;  /* next unread byte */
+} walk;
 
-static const uint8_t *take(cursor *c, size_t n) {
-    if (c->broken || n > c->size - c->at) {
-        c->broken = 1;
-        return NULL;
-    }
-    const uint8_t *p = c->buf + c->at;
-    c->at += n;
-    return p;
-}
+static int fits(const walk *w, uint64_t n) { return n <= (uint64_t)(w->size - w->pos); }
 
-static uint32_t le32(const uint8_t *p) {
+static uint32_t load_le32(const uint8_t *p) {
     return (uint32_t)p[0] | (uint32_t)p[1] << 8 | (uint32_t)p[2] << 16 | (uint32_t)p[3] << 24;
 }
+static uint64_t load_le64(const uint8_t *p) { return (uint64_t)load_le32(p) | (uint64_t)load_le32(p + 4) << 32; }
 
-static uint32_t take_u32(cursor *c) {
-    const uint8_t *p = take(c, 4);
-    return p ? le32(p) : 0;
+/* each reader advances only over bytes that are there; 0 on success */
+static int get_u32(walk *w, uint32_t *v) {
+    if (!fits(w, 4)) return -1;
+    *v = load_le32(w->base + w->pos);
+    w->pos += 4;
+    return 0;
+}
+static int get_u64(walk *w, uint64_t *v) {
+    if (!fits(w, 8)) return -1;
+    *v = load_le64(w->base + w->pos);
+    w->pos += 8;
+    return 0;
+}
+static int get_span(walk *w, uint64_t n, const uint8_t **p) {
+    if (!fits(w, n)) return -1;
+    *p = w->base + w->pos;
+    w->pos += (size_t)n;
+    return 0;
+}
+/* u32 length + bytes into dst[cap] as a C string: 1..cap-1 bytes, none of them NUL */
+static int get_name(walk *w, char *dst, size_t cap) {
+    uint32_t n;
+    const uint8_t *s;
+    if (get_u32(w, &n) || n == 0 || n >= cap || get_span(w, n, &s) || memchr(s, 0, n)) return -1;
+    memcpy(dst, s, n);
+    dst[n] = '\0';
+    return 0;
 }
 
-static uint64_t take_u64(cursor *c) {
-    const uint64_t lo = take_u32(c), hi = take_u32(c);
-    return lo | (hi << 32);
-}
-
-static int errf(char *err, size_t errlen, const char *fmt, ...) {
+static int say(char *err, size_t errlen, const char *fmt, ...) {
     if (err && errlen) {
         va_list ap;
         va_start(ap, fmt);
@@ -53,110 +85,113 @@ static int errf(char *err, size_t errlen, const char *fmt, ...) {
     return -1;
 }
 
-/* length-prefixed name into dst[cap]: 1..cap-1 bytes, no embedded NUL */
-static int take_name(cursor *c, char *dst, size_t cap) {
-    const uint32_t n = take_u32(c);
-    if (c->broken || n == 0 || n >= cap) return -1;
-    const uint8_t *s = take(c, n);
-    if (!s || memchr(s, 0, n)) return -1;
-    memcpy(dst, s, n);
-    dst[n] = 0;
-    return 0;
+/* one key/value entry */
+static int parse_entry(walk *w, qlm_kv *kv) {
+    uint32_t raw;
+    if (get_name(w, kv->key, sizeof kv->key) || get_u32(w, &kv->type)) return -1;
+    switch (kv->type) {
+    case QLM_KV_U32: return get_u32(w, &kv->u32);
+    case QLM_KV_F32:
+        if (get_u32(w, &raw)) return -1;
+        memcpy(&kv->f32, &raw, sizeof raw);
+        return 0;
+    case QLM_KV_STR: return get_u32(w, &kv->len) || get_span(w, kv->len, (const uint8_t **)&kv->str);
+    case QLM_KV_ARR_U32: return get_u32(w, &kv->len) || get_span(w, (uint64_t)kv->len * 4, &kv->arr);
+    default: return -1;
+    }
+}
+
+/* one tensor entry up to its offset (the range check against the data region is the caller's) */
+static int parse_tensor(walk *w, qm_tensor *t, uint64_t *off) {
+    uint32_t dt, nd;
+    if (get_name(w, t->name, sizeof t->name) || get_u32(w, &dt) || get_u32(w, &nd)) return -1;
+    if (!qm_dtype_valid(dt) || nd < 1 || nd > 4) return -1;
+    t->type = (qm_dtype)dt;
+    t->ndim = (int)nd;
+    uint64_t elems = 1;
+    for (uint32_t d = 0; d < nd; d++) {
+        uint64_t ne;
+        if (get_u64(w, &ne) || ne == 0 || ne > QLM_MAX_ELEMS || elems > QLM_MAX_ELEMS / ne) return -1;
+        elems *= ne;
+        t->ne[d] = (int64_t)ne;
+    }
+    return get_u64(w, off) || *off % QM_ALIGN != 0 ? -1 : 0;
 }
 
 int qlm_parse(qlm_file *f, const uint8_t *buf, size_t size, char *err, size_t errlen) {
     memset(f, 0, sizeof *f);
-    cursor c = {buf, size, 0, 0};
-    const uint8_t *magic = take(&c, 4);
-    if (!magic || memcmp(magic, QLM_MAGIC, 4) != 0) return errf(err, errlen, "bad magic");
-    const uint32_t version = take_u32(&c);
-    if (version != QLM_VERSION) return errf(err, errlen, "unsupported version %u", version);
-    const uint32_t n_kv = take_u32(&c), n_t = take_u32(&c);
-    const uint64_t data_off = take_u64(&c);
-    if (c.broken) return errf(err, errlen, "truncated header");
-    if (n_kv > QLM_MAX_KV || n_t > QLM_MAX_TENSORS) return errf(err, errlen, "too many entries");
-    if (data_off % QM_ALIGN || data_off > size) return errf(err, errlen, "bad data offset");
-    f->kv = calloc(n_kv ? n_kv : 1, sizeof *f->kv);
-    f->tensors = calloc(n_t ? n_t : 1, sizeof *f->tensors);
-    if (!f->kv || !f->tensors) {
-        qlm_close(f);
-        return errf(err, errlen, "out of memory");
+    if (size < 4 || memcmp(buf, QLM_MAGIC, 4) != 0) return say(err, errlen, "bad magic");
+    if (size < 8) return say(err, errlen, "file ends inside the %u-byte header prelude", QLM_PRELUDE_BYTES);
+    const uint32_t version = load_le32(buf + 4);
+    if (version != QLM_VERSION) return say(err, errlen, "unsupported version %u", version);
+    if (size < QLM_PRELUDE_BYTES)
+        return say(err, errlen, "file ends inside the %u-byte header prelude", QLM_PRELUDE_BYTES);
+    const uint32_t n_kv = load_le32(buf + 8), n_t = load_le32(buf + 12);
+    const uint64_t data_off = load_le64(buf + 16);
+    if (n_kv > QLM_MAX_KV || n_t > QLM_MAX_TENSORS)
+        return say(err, errlen, "header declares %u key/value entries and %u tensors (limits %d and %d)", n_kv, n_t,
+                   QLM_MAX_KV, QLM_MAX_TENSORS);
+    if (data_off % QM_ALIGN != 0 || data_off > size)
+        return say(err, errlen, "data offset %llu is not a multiple of %d or lies past the end of the %zu-byte file",
+                   (unsigned long long)data_off, QM_ALIGN, size);
+
+    qlm_kv *kv = calloc(n_kv ? n_kv : 1, sizeof *kv);
+    qm_tensor *tn = calloc(n_t ? n_t : 1, sizeof *tn);
+    if (!kv || !tn) {
+        free(kv);
+        free(tn);
+        return say(err, errlen, "out of memory for %u entries and %u tensors", n_kv, n_t);
     }
-    f->n_kv = n_kv;
-    f->n_tensors = n_t;
+    f->kv = kv, f->tensors = tn, f->n_kv = n_kv, f->n_tensors = n_t;
+
+    walk w = {buf, size, QLM_PRELUDE_BYTES};
     for (uint32_t i = 0; i < n_kv; i++) {
-        qlm_kv *kv = &f->kv[i];
-        if (take_name(&c, kv->key, sizeof kv->key)) goto malformed;
-        kv->type = take_u32(&c);
-        if (kv->type == QLM_KV_U32) {
-            kv->u32 = take_u32(&c);
-        } else if (kv->type == QLM_KV_F32) {
-            const uint32_t b = take_u32(&c);
-            memcpy(&kv->f32, &b, 4);
-        } else if (kv->type == QLM_KV_STR) {
-            kv->len = take_u32(&c);
-            kv->str = (const char *)take(&c, kv->len);
-        } else if (kv->type == QLM_KV_ARR_U32) {
-            kv->len = take_u32(&c);
-            if (!c.broken && kv->len > (size - c.at) / 4) goto malformed;
-            kv->arr = take(&c, (size_t)kv->len * 4);
-        } else {
-            goto malformed;
+        const size_t at = w.pos;
+        if (parse_entry(&w, &kv[i])) {
+            qlm_close(f);
+            return say(err, errlen, "key/value entry %u (at byte %zu) is malformed or truncated", i, at);
         }
-        if (c.broken) goto malformed;
     }
-    const size_t data_bytes = size - (size_t)data_off;
+    const uint64_t data_bytes = size - (size_t)data_off;
     for (uint32_t i = 0; i < n_t; i++) {
-        qm_tensor *t = &f->tensors[i];
-        if (take_name(&c, t->name, sizeof t->name)) goto malformed;
-        const uint32_t dt = take_u32(&c), nd = take_u32(&c);
-        if (c.broken || !qm_dtype_valid(dt) || nd < 1 || nd > 4) goto malformed;
-        t->type = (qm_dtype)dt;
-        t->ndim = (int)nd;
-        uint64_t total = 1;
-        const uint64_t cap = (uint64_t)1 << 40;
-        for (uint32_t d = 0; d < nd; d++) {
-            const uint64_t ne = take_u64(&c);
-            if (ne == 0 || ne > cap || total > cap / ne) goto malformed;
-            total *= ne;
-            t->ne[d] = (int64_t)ne;
+        const size_t at = w.pos;
+        uint64_t off = 0;
+        if (parse_tensor(&w, &tn[i], &off)) {
+            qlm_close(f);
+            return say(err, errlen, "tensor entry %u (at byte %zu) is malformed or truncated", i, at);
         }
-        const uint64_t off = take_u64(&c);
-        if (c.broken || off % QM_ALIGN) goto malformed;
-        const size_t bytes = qm_tensor_bytes(t);
+        const uint64_t bytes = qm_tensor_bytes(&tn[i]);
         if (off > data_bytes || bytes > data_bytes - off) {
-            errf(err, errlen, "tensor '%s' out of range", t->name);
+            say(err, errlen, "tensor '%s' (%llu bytes at data offset %llu) lies outside the %llu-byte data region",
+                tn[i].name, (unsigned long long)bytes, (unsigned long long)off, (unsigned long long)data_bytes);
             qlm_close(f);
             return -1;
         }
-        t->data = buf + data_off + off;
+        tn[i].data = buf + data_off + off;
     }
-    if (c.at > data_off) goto malformed; /* header runs into the data */
+    if (w.pos > data_off) {
+        qlm_close(f);
+        return say(err, errlen, "header (%zu bytes) runs into the data at byte %llu", w.pos, (unsigned long long)data_off);
+    }
     return 0;
-malformed:
-    qlm_close(f);
-    return errf(err, errlen, "malformed header near byte %zu", c.at);
 }
 
 int qlm_open(qlm_file *f, const char *path, char *err, size_t errlen) {
     memset(f, 0, sizeof *f);
     const int fd = open(path, O_RDONLY);
-    if (fd < 0) return errf(err, errlen, "cannot open %s", path);
+    if (fd < 0) return say(err, errlen, "cannot open %s: %s", path, strerror(errno));
     struct stat st;
-    if (fstat(fd, &st) != 0 || st.st_size <= 0) {
-        close(fd);
-        return errf(err, errlen, "cannot stat %s", path);
-    }
-    const size_t size = (size_t)st.st_size;
-    void *map = mmap(NULL, size, PROT_READ, MAP_PRIVATE, fd, 0);
-    close(fd);
-    if (map == MAP_FAILED) return errf(err, errlen, "mmap failed");
-    if (qlm_parse(f, map, size, err, errlen) != 0) {
-        munmap(map, size);
+    const int stat_ok = fstat(fd, &st) == 0 && st.st_size > 0;
+    void *map = stat_ok ? mmap(NULL, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0) : MAP_FAILED;
+    close(fd); /* the mapping keeps the file's pages */
+    if (!stat_ok) return say(err, errlen, "%s is empty or cannot be inspected", path);
+    if (map == MAP_FAILED) return say(err, errlen, "cannot map %s: %s", path, strerror(errno));
+    if (qlm_parse(f, map, (size_t)st.st_size, err, errlen) != 0) {
+        munmap(map, (size_t)st.st_size);
         return -1;
     }
     f->map = map;
-    f->map_size = size;
+    f->map_size = (size_t)st.st_size;
     return 0;
 }
 
@@ -169,14 +204,14 @@ void qlm_close(qlm_file *f) {
 
 const qlm_kv *qlm_find_kv(const qlm_file *f, const char *key) {
     for (uint32_t i = 0; i < f->n_kv; i++)
-        if (!strcmp(f->kv[i].key, key)) return &f->kv[i];
+        if (strcmp(f->kv[i].key, key) == 0) return &f->kv[i];
     return NULL;
 }
 
 const qm_tensor *qlm_find_tensor(const qlm_file *f, const char *name) {
     for (uint32_t i = 0; i < f->n_tensors; i++)
-        if (!strcmp(f->tensors[i].name, name)) return &f->tensors[i];
+        if (strcmp(f->tensors[i].name, name) == 0) return &f->tensors[i];
     return NULL;
 }
 
-uint32_t qlm_arr_get(const qlm_kv *kv, uint32_t i) { return le32(kv->arr + (size_t)i * 4); }
+uint32_t qlm_arr_get(const qlm_kv *kv, uint32_t i) { return load_le32(kv->arr + (size_t)i * 4); }
