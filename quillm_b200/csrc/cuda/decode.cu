@@ -147,11 +147,20 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsi
 __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, bool dead) {
+// publish_ss: the phase that ends wrote x (a residual phase); its warps left their sums of squares in
+// shared memory, and thread 0 stores the CTA's total (warp order) before it arrives
+__device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, bool dead, bool publish_ss) {
     int *flag = (int *)(sm + p.off_red + kRedFlag);
     named_sync(kBarConsumers, NCT);
     if (threadIdx.x == 0) {
         int ok = 1;
+        if (publish_ss) {
+            const double *dred = (const double *)(sm + p.off_red + kRedDred);
+            double tot = 0.0;
+#pragma unroll
+            for (int k = 0; k < NCW; k++) tot += dred[k];
+            __stcg(p.ssq + blockIdx.x, tot);
+        }
         DTRACE_SET((int)(target / gridDim.x) - 1, kTrArrive, gtime());
         red_release_add(p.gbar, 1u);
         if (!dead && !counter_wait(p.gbar, target)) {
@@ -475,56 +484,89 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
 
 // The phase input quantized into shared memory by the consumer threads, two per block: one loop over the
 // rounds of QPR blocks, with one load site and one quantization site for every kind of phase, so the
-// instruction footprint the SMs cycle through each layer stays small:
+// instruction footprint the SMs cycle through each layer stays small; the next round's input is loaded
+// while the current one is quantized.
 //  - rmsnorm phases (QKV, FFN, OUT): x * inv * w, inv = (float)(1 / sqrt(sum_double(x^2)/n + eps))
-//    (src/ops.c:93-98), x the residual stream or, in the step's first phase, the token's embedding
-//    (which CTA 0 also stores into x).  With one round, x and w are loaded together and x stays in
-//    registers across the block sum; longer rows take a first pass for the sum;
+//    (src/ops.c:93-98).  The sum of squares comes from the per-CTA partials the residual phase that
+//    wrote x left in p.ssq (every warp adds them in the same order); in the step's first phase, where x
+//    is the token's embedding (which CTA 0 also stores into x), the CTA sums its own loads: with one
+//    round x stays in registers across the block sum, longer rows take a first pass for the sum;
 //  - WO: the attention output, merged from the segment partials;
 //  - W2: the SwiGLU output.
 // Threads past the row's blocks load zeros and store nothing.
+constexpr int kSsLoads = kDecodeMaxGrid / 32;  // per-CTA partials each lane loads
+__device__ __forceinline__ void prologue_load(const DecodeParams &p, const DecodePhase &ph, const uint8_t *erow, int nseg,
+                                              int64_t e0, float (&v)[16]) {
+    if (erow) embed16(p, erow, e0, ph.K, v);
+    else if (ph.kind == PH_WO) attn_out16(p, e0, ph.K, nseg, v);
+    else load16<true>(ph.in, e0, ph.K, v);
+}
+
 __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int token, int pos) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, qd = t >> 1, j = t & 1;
     uint8_t *xq = sm + p.off_xq;
     int2 *xds = (int2 *)(sm + p.off_xds);
     const bool q4 = ph.dtype == QMC_Q4_0, norm = ph.norm_w != nullptr;
     const int K = ph.K, rounds = (ph.nb + QPR - 1) / QPR;
-    const bool two_pass = norm && rounds > 1;  // a sum pass over all rounds, then the quantizing pass
     const uint8_t *erow = ph.embed ? p.tok + (int64_t)token * row_bytes(p.dt_tok, K) : nullptr;
-    const bool keep_x = ph.embed && blockIdx.x == 0;
+    const bool own_ss = norm && erow;           // embedding input: the CTA sums its own squares
+    const bool two_pass = own_ss && rounds > 1;  // ... in a first pass when the row takes several rounds
+    const bool keep_x = erow && blockIdx.x == 0;
     const int nseg = ph.kind == PH_WO ? attn_segments(p, pos) : 0;
-    double ss = 0.0;
     float inv = 1.0f;
+    if (two_pass) {
+        double ss = 0.0;
 #pragma unroll 1
-    for (int it = 0; it < (two_pass ? 2 * rounds : rounds); it++) {
-        const bool sum_pass = two_pass && it < rounds;
-        const int r = two_pass && !sum_pass ? it - rounds : it;
-        const int b = r * QPR + qd;
-        const int64_t e0 = (int64_t)b * 32 + 16 * j;
-        float v[16], w[16];
-        if (erow) embed16(p, erow, e0, K, v);
-        else if (ph.kind == PH_WO) attn_out16(p, e0, K, nseg, v);
-        else load16<true>(ph.in, e0, K, v);
-        if (norm && !sum_pass) load16<false>(ph.norm_w, e0, K, w);  // in flight with v
-        if (norm && (sum_pass || !two_pass)) {
+        for (int r = 0; r < rounds; r++) {
+            float v[16];
+            prologue_load(p, ph, erow, nseg, (int64_t)(r * QPR + qd) * 32 + 16 * j, v);
 #pragma unroll
             for (int i = 0; i < 16; i++) ss = fma((double)v[i], (double)v[i], ss);
-            if (it == rounds - 1) {  // the block's sum, same order in every warp
-                ss = warp_sum_d(ss);
-                double *dred = (double *)(sm + p.off_red + kRedDred);
-                if (lane == 0) dred[warp] = ss;
-                named_sync(kBarConsumers, NCT);
-                float invl = 0.0f;
-                if (lane == 0) {  // one lane per warp: double division and sqrt are slow
-                    double tot = 0.0;
-#pragma unroll
-                    for (int k = 0; k < NCW; k++) tot += dred[k];
-                    invl = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
-                }
-                inv = __shfl_sync(0xffffffffu, invl, 0);
-            }
         }
-        if (sum_pass) continue;
+        ss = warp_sum_d(ss);
+        double *dred = (double *)(sm + p.off_red + kRedDred);
+        if (lane == 0) dred[warp] = ss;
+        named_sync(kBarConsumers, NCT);
+        double tot = 0.0;
+#pragma unroll
+        for (int k = 0; k < NCW; k++) tot += dred[k];
+        inv = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
+        named_sync(kBarConsumers, NCT);  // dred is free again
+    }
+    // w: the norm weights, or (phases without a norm) the next round's input, loaded while the current
+    // round is quantized
+    float v[16], w[16];
+    prologue_load(p, ph, erow, nseg, (int64_t)qd * 32 + 16 * j, v);
+    if (norm) load16<false>(ph.norm_w, (int64_t)qd * 32 + 16 * j, K, w);
+    else if (rounds > 1) prologue_load(p, ph, erow, nseg, (int64_t)(QPR + qd) * 32 + 16 * j, w);
+    if (norm && !own_ss) {  // the partials, in flight together with the first rounds' input
+        double sp = 0.0;
+#pragma unroll
+        for (int c = 0; c < kSsLoads; c++) sp += lane + 32 * c < (int)gridDim.x ? __ldcg(p.ssq + lane + 32 * c) : 0.0;
+        const double tot = warp_sum_d(sp);
+        inv = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
+    }
+#pragma unroll 1
+    for (int r = 0; r < rounds; r++) {
+        const int b = r * QPR + qd;
+        const int64_t e0 = (int64_t)b * 32 + 16 * j;
+        if (own_ss && !two_pass) {  // one round: the block sum of the registers' squares
+            double ss = 0.0;
+#pragma unroll
+            for (int i = 0; i < 16; i++) ss = fma((double)v[i], (double)v[i], ss);
+            ss = warp_sum_d(ss);
+            double *dred = (double *)(sm + p.off_red + kRedDred);
+            if (lane == 0) dred[warp] = ss;
+            named_sync(kBarConsumers, NCT);
+            float invl = 0.0f;
+            if (lane == 0) {  // one lane per warp: double division and sqrt are slow
+                double tot = 0.0;
+#pragma unroll
+                for (int k = 0; k < NCW; k++) tot += dred[k];
+                invl = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
+            }
+            inv = __shfl_sync(0xffffffffu, invl, 0);
+        }
         if (keep_x) {
 #pragma unroll
             for (int i = 0; i < 16; i++)
@@ -535,6 +577,16 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
             for (int i = 0; i < 16; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
         }
         quant_block(q4, xq, xds, b, j, b < ph.nb, v);
+        if (r + 1 < rounds) {
+            if (norm) {
+                prologue_load(p, ph, erow, nseg, e0 + QPR * 32, v);
+                load16<false>(ph.norm_w, e0 + QPR * 32, K, w);
+            } else {  // round r + 1 is in w; round r + 2 goes in flight
+#pragma unroll
+                for (int i = 0; i < 16; i++) v[i] = w[i];
+                if (r + 2 < rounds) prologue_load(p, ph, erow, nseg, e0 + 2 * QPR * 32, w);
+            }
+        }
     }
     named_sync(kBarConsumers, NCT);
 }
@@ -601,7 +653,7 @@ __device__ __forceinline__ float2 epilogue_operand(const DecodeParams &p, const 
 
 template <bool KV16>
 __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhase &ph, int64_t unit, float a, float b,
-                                         float2 opnd, int pos, unsigned long long &best) {
+                                         float2 opnd, int pos, unsigned long long &best, double &ss) {
     switch (ph.kind) {
     case PH_QKV: {  // rows 2u, 2u+1: one RoPE pair of q or k, or two v values
         const int64_t vr = 2 * unit;
@@ -630,7 +682,12 @@ __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhas
         break;
     }
     case PH_WO:
-    case PH_W2: __stcg(ph.out + unit, opnd.x + a); break;  // residual (src/model.c:179,186)
+    case PH_W2: {  // residual (src/model.c:179,186); its square goes into the next rmsnorm's sum
+        const float y = opnd.x + a;
+        __stcg(ph.out + unit, y);
+        ss = fma((double)y, (double)y, ss);
+        break;
+    }
     case PH_FFN: __stcg(ph.out + unit, __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), b)); break;  // src/ops.c:128-133
     default:  // PH_OUT
         __stcg(ph.out + unit, a);
@@ -723,12 +780,22 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         if (GW == 1 && k < nst && unit < u1) opre = epilogue_operand(p, ph, unit, pos);
     }
     bool first_batch = GW == 1;
+    // residual phases: the warp's sum of the squares of the x values it stores, kept in shared memory
+    // (grid_sync publishes the CTA's total) so that no double stays live across the stage loop
+    double *wss = (double *)(sm + p.off_red + kRedDred) + warp;
+    const bool resid = ph.kind == PH_WO || ph.kind == PH_W2;
+    if (resid && lane == 0) *wss = 0.0;
     auto flush = [&]() {
         const unsigned long long tf = trace_slot(phi, kTrFlush) ? clock64() : 0;
         nunits += npend;
+        double ss = 0.0;
         if (lane < npend) {
             const float2 opnd = first_batch ? opre : epilogue_operand(p, ph, punit, pos);
-            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best);
+            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best, ss);
+        }
+        if (resid) {
+            ss = warp_sum_d(ss);
+            if (lane == 0) *wss += ss;
         }
         npend = 0;
         first_batch = false;
@@ -772,6 +839,7 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
     }
     if (!dead) flush();
     gk += (unsigned)nst;
+
     if (lane == 0) {
         DTRACE_ADD(phi, kTrFullWait, twait);
         DTRACE_ADD(phi, kTrFlush, tflush);
@@ -1037,8 +1105,9 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
     named_sync(kBarConsumers, NCT);
     for (int i = 0; i < p.nph; i++) {
         if (i > 0) {
+            const int prev = dsm[(i - 1) & 1].kind;  // read before the barrier publishes phase i's descriptor
             desc_wait();  // phase i's descriptor (copied during phase i - 1); the barrier publishes it
-            if (!grid_sync(p, sm, (unsigned)i * gridDim.x, dead)) dead = true;
+            if (!grid_sync(p, sm, (unsigned)i * gridDim.x, dead, prev == PH_WO || prev == PH_W2)) dead = true;
         }
         const DecodePhase &ph = dsm[i & 1];
         if (t == 0) DTRACE_SET(i, kTrStart, gtime());
