@@ -86,6 +86,9 @@ enum : int {
     kTrUnits,      // units the CTA's warps computed
     kTrFlush,      // consumer warps' time in epilogue flushes (cycles, summed)
     kTrDot,        // consumer warps' time in row dots (cycles, summed)
+    kTrProLoad,    // thread 0's first prologue loads (or attention's q) have landed
+    kTrAttnKV,     // attention: thread 0's first K/V chunk has landed
+    kTrAttnLoop,   // attention: warp 0 left its position loop
     kTrSlots = 16
 };
 __device__ __forceinline__ unsigned long long gtime() {
@@ -147,20 +150,11 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsi
 __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// publish_ss: the phase that ends wrote x (a residual phase); its warps left their sums of squares in
-// shared memory, and thread 0 stores the CTA's total (warp order) before it arrives
-__device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, bool dead, bool publish_ss) {
+__device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, bool dead) {
     int *flag = (int *)(sm + p.off_red + kRedFlag);
     named_sync(kBarConsumers, NCT);
     if (threadIdx.x == 0) {
         int ok = 1;
-        if (publish_ss) {
-            const double *dred = (const double *)(sm + p.off_red + kRedDred);
-            double tot = 0.0;
-#pragma unroll
-            for (int k = 0; k < NCW; k++) tot += dred[k];
-            __stcg(p.ssq + blockIdx.x, tot);
-        }
         DTRACE_SET((int)(target / gridDim.x) - 1, kTrArrive, gtime());
         red_release_add(p.gbar, 1u);
         if (!dead && !counter_wait(p.gbar, target)) {
@@ -487,14 +481,12 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
 // instruction footprint the SMs cycle through each layer stays small; the next round's input is loaded
 // while the current one is quantized.
 //  - rmsnorm phases (QKV, FFN, OUT): x * inv * w, inv = (float)(1 / sqrt(sum_double(x^2)/n + eps))
-//    (src/ops.c:93-98).  The sum of squares comes from the per-CTA partials the residual phase that
-//    wrote x left in p.ssq (every warp adds them in the same order); in the step's first phase, where x
-//    is the token's embedding (which CTA 0 also stores into x), the CTA sums its own loads: with one
-//    round x stays in registers across the block sum, longer rows take a first pass for the sum;
+//    (src/ops.c:93-98), x the residual stream or, in the step's first phase, the token's embedding
+//    (which CTA 0 also stores into x).  With one round, x and w are loaded together and x stays in
+//    registers across the block sum; longer rows take a first pass for the sum;
 //  - WO: the attention output, merged from the segment partials;
 //  - W2: the SwiGLU output.
 // Threads past the row's blocks load zeros and store nothing.
-constexpr int kSsLoads = kDecodeMaxGrid / 32;  // per-CTA partials each lane loads
 __device__ __forceinline__ void prologue_load(const DecodeParams &p, const DecodePhase &ph, const uint8_t *erow, int nseg,
                                               int64_t e0, float (&v)[16]) {
     if (erow) embed16(p, erow, e0, ph.K, v);
@@ -502,14 +494,14 @@ __device__ __forceinline__ void prologue_load(const DecodeParams &p, const Decod
     else load16<true>(ph.in, e0, ph.K, v);
 }
 
-__device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int token, int pos) {
+__device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int token, int pos, int phi) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, qd = t >> 1, j = t & 1;
     uint8_t *xq = sm + p.off_xq;
     int2 *xds = (int2 *)(sm + p.off_xds);
     const bool q4 = ph.dtype == QMC_Q4_0, norm = ph.norm_w != nullptr;
     const int K = ph.K, rounds = (ph.nb + QPR - 1) / QPR;
     const uint8_t *erow = ph.embed ? p.tok + (int64_t)token * row_bytes(p.dt_tok, K) : nullptr;
-    const bool own_ss = norm && erow;           // embedding input: the CTA sums its own squares
+    const bool own_ss = norm;                    // the CTA sums the squares of its loads
     const bool two_pass = own_ss && rounds > 1;  // ... in a first pass when the row takes several rounds
     const bool keep_x = erow && blockIdx.x == 0;
     const int nseg = ph.kind == PH_WO ? attn_segments(p, pos) : 0;
@@ -539,13 +531,7 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
     prologue_load(p, ph, erow, nseg, (int64_t)qd * 32 + 16 * j, v);
     if (norm) load16<false>(ph.norm_w, (int64_t)qd * 32 + 16 * j, K, w);
     else if (rounds > 1) prologue_load(p, ph, erow, nseg, (int64_t)(QPR + qd) * 32 + 16 * j, w);
-    if (norm && !own_ss) {  // the partials, in flight together with the first rounds' input
-        double sp = 0.0;
-#pragma unroll
-        for (int c = 0; c < kSsLoads; c++) sp += lane + 32 * c < (int)gridDim.x ? __ldcg(p.ssq + lane + 32 * c) : 0.0;
-        const double tot = warp_sum_d(sp);
-        inv = (float)(1.0 / sqrt(tot / (double)K + (double)p.eps));
-    }
+    if (t == 0) DTRACE_SET(phi, kTrProLoad, gtime_after(v[0] + w[0]));
 #pragma unroll 1
     for (int r = 0; r < rounds; r++) {
         const int b = r * QPR + qd;
@@ -653,7 +639,7 @@ __device__ __forceinline__ float2 epilogue_operand(const DecodeParams &p, const 
 
 template <bool KV16>
 __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhase &ph, int64_t unit, float a, float b,
-                                         float2 opnd, int pos, unsigned long long &best, double &ss) {
+                                         float2 opnd, int pos, unsigned long long &best) {
     switch (ph.kind) {
     case PH_QKV: {  // rows 2u, 2u+1: one RoPE pair of q or k, or two v values
         const int64_t vr = 2 * unit;
@@ -682,12 +668,7 @@ __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhas
         break;
     }
     case PH_WO:
-    case PH_W2: {  // residual (src/model.c:179,186); its square goes into the next rmsnorm's sum
-        const float y = opnd.x + a;
-        __stcg(ph.out + unit, y);
-        ss = fma((double)y, (double)y, ss);
-        break;
-    }
+    case PH_W2: __stcg(ph.out + unit, opnd.x + a); break;  // residual (src/model.c:179,186)
     case PH_FFN: __stcg(ph.out + unit, __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), b)); break;  // src/ops.c:128-133
     default:  // PH_OUT
         __stcg(ph.out + unit, a);
@@ -780,22 +761,12 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         if (GW == 1 && k < nst && unit < u1) opre = epilogue_operand(p, ph, unit, pos);
     }
     bool first_batch = GW == 1;
-    // residual phases: the warp's sum of the squares of the x values it stores, kept in shared memory
-    // (grid_sync publishes the CTA's total) so that no double stays live across the stage loop
-    double *wss = (double *)(sm + p.off_red + kRedDred) + warp;
-    const bool resid = ph.kind == PH_WO || ph.kind == PH_W2;
-    if (resid && lane == 0) *wss = 0.0;
     auto flush = [&]() {
         const unsigned long long tf = trace_slot(phi, kTrFlush) ? clock64() : 0;
         nunits += npend;
-        double ss = 0.0;
         if (lane < npend) {
             const float2 opnd = first_batch ? opre : epilogue_operand(p, ph, punit, pos);
-            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best, ss);
-        }
-        if (resid) {
-            ss = warp_sum_d(ss);
-            if (lane == 0) *wss += ss;
+            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best);
         }
         npend = 0;
         first_batch = false;
@@ -878,7 +849,7 @@ __device__ void attn_prefetch(const DecodeParams &p, const DecodePhase &ph, int 
 }
 
 template <typename KT>  // cache element: float or __half
-__device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int pos) {
+__device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, int pos, int phi) {
     constexpr bool F16 = std::is_same<KT, __half>::value;
     constexpr int CH = F16 ? 2 * kAttnChunk : kAttnChunk;  // positions per warp loaded together
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -904,7 +875,9 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
             o[g][w] = 0.0f;
         }
     }
+    if (t == 0) DTRACE_SET(phi, kTrProLoad, gtime_after(q[0][0]));
     // positions t0 + warp, + NCW, ...: the K and V rows of up to CH of them are loaded at once
+    bool first_chunk = true;
     for (int tb = t0 + warp; tb < t1; tb += CH * NCW) {
         float k[CH][MAXW], v[CH][MAXW];
         if constexpr (F16) {
@@ -940,6 +913,8 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
                 }
             }
         }
+        if (t == 0 && first_chunk) DTRACE_SET(phi, kTrAttnKV, gtime_after(k[0][0] + v[0][0]));
+        first_chunk = false;
         if constexpr (!F16) {  // fp32 cache: one online softmax update per position
 #pragma unroll
             for (int c = 0; c < CH; c++) {
@@ -1002,6 +977,7 @@ __device__ void attention(const DecodeParams &p, const DecodePhase &ph, uint8_t 
             }
         }
     }
+    if (t == 0) DTRACE_SET(phi, kTrAttnLoop, gtime_after(l[0]));
     // merge the warps in one pass (the activation area is free during attention): every warp's (max, sum)
     // and acc per query head go to shared memory, then each consumer thread merges one (head, dimension)
     // over the NCW warps in warp order -- one CTA barrier instead of a tree of them -- and writes this
@@ -1105,20 +1081,19 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
     named_sync(kBarConsumers, NCT);
     for (int i = 0; i < p.nph; i++) {
         if (i > 0) {
-            const int prev = dsm[(i - 1) & 1].kind;  // read before the barrier publishes phase i's descriptor
             desc_wait();  // phase i's descriptor (copied during phase i - 1); the barrier publishes it
-            if (!grid_sync(p, sm, (unsigned)i * gridDim.x, dead, prev == PH_WO || prev == PH_W2)) dead = true;
+            if (!grid_sync(p, sm, (unsigned)i * gridDim.x, dead)) dead = true;
         }
         const DecodePhase &ph = dsm[i & 1];
         if (t == 0) DTRACE_SET(i, kTrStart, gtime());
         if (i + 1 < p.nph) desc_prefetch(p.ph + i + 1, dsm + ((i + 1) & 1));
         if (ph.kind == PH_ATTN) {
-            if constexpr (KV16) attention<__half>(p, ph, sm, pos);
-            else attention<float>(p, ph, sm, pos);
+            if constexpr (KV16) attention<__half>(p, ph, sm, pos, i);
+            else attention<float>(p, ph, sm, pos, i);
             if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
             continue;
         }
-        prologue(p, ph, sm, token, pos);
+        prologue(p, ph, sm, token, pos, i);
         if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
         unsigned long long best = 0;  // this thread's argmax key (OUT phase)
         const bool two = ph.urows == 2;

@@ -17,7 +17,6 @@ int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, voi
                         cudaStream_t s);
 
 constexpr int kDecodeHeadsPerUnit = 4;  // query heads per attention work unit
-constexpr int kDecodeMaxGrid = 160;     // CTAs (one per SM) whose sum-of-squares partials a prologue reads
 constexpr int kDecodePartHead = 4;      // floats before acc[] in an attention segment partial
 
 enum DecodePhaseKind : int { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_W2 = 4, PH_OUT = 5 };
@@ -45,7 +44,6 @@ struct DecodeParams {
     const uint8_t *tok;  // embedding table (file layout)
     int dt_tok;
     float *x;  // residual stream
-    double *ssq;  // per-CTA sums of squares of x, written by the residual (wo / w2) phases [gridDim.x]
     float *q;
     float *logits;
     const float2 *rope;

@@ -14,6 +14,7 @@
 // ranks store theirs, then one in-place sum all-reduce of D floats gives x + sum of partials everywhere.
 #include <nccl.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -73,7 +74,6 @@ struct qmc_model {
     DecodePhase *d_phases = nullptr;
     uint8_t *sout = nullptr;
     unsigned *gbar = nullptr;
-    double *ssq = nullptr;  // per-CTA sums of squares of x (written by the residual phases)
     float *apart = nullptr;
     int maxseg = 1, gsplit = 1;
     // batched prompt forward: row buffers for up to pf_cap tokens (allocated on first use, grown on demand)
@@ -240,7 +240,7 @@ int nccl_check(ncclResult_t r, const char *what) {
 // ---------------------------------------------------------------- persistent decode path
 // Eligible when one GPU holds the model, every matrix is Q8_0/Q4_0 and the ring plan fits shared memory.
 bool decode_eligible(qmc_model *m, DevCtx *c) {
-    if (m->tp != 1 || m->hd > 128 || c->num_sms > kDecodeMaxGrid) return false;
+    if (m->tp != 1 || m->hd > 128) return false;
     auto q = [](int dt) { return dt == QMC_Q8_0 || dt == QMC_Q4_0; };
     if (!q(m->dt_out)) return false;
     int64_t umax = split_row_bytes(m->dt_out, m->D);
@@ -362,7 +362,6 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
         const size_t units = (size_t)m->NKVl * m->gsplit;
         RC(dalloc(m, (void **)&m->d_phases, m->phases.size() * sizeof(DecodePhase)));
         RC(dalloc(m, (void **)&m->gbar, 64));
-        RC(dalloc(m, (void **)&m->ssq, (size_t)c->num_sms * sizeof(double)));
         RC(dalloc(m, (void **)&m->apart, units * m->maxseg * kDecodeHeadsPerUnit * (m->hd + kDecodePartHead) * 4));
         QMC_CUDA(cudaMemcpy(m->d_phases, m->phases.data(), m->phases.size() * sizeof(DecodePhase), cudaMemcpyHostToDevice));
         QMC_CUDA(cudaMemset(m->gbar, 0, 64));
@@ -383,7 +382,6 @@ int launch_decode_step(qmc_model *m, DevCtx *c) {
     p.tok = m->tok;
     p.dt_tok = m->dt_tok;
     p.x = m->x, p.q = m->q, p.logits = m->logits;
-    p.ssq = m->ssq;
     p.rope = m->rope;
     p.state = m->state, p.forced = m->forced, p.gen = m->gen, p.gen_cap = m->S;
     p.vocab = m->V;

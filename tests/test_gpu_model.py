@@ -137,12 +137,24 @@ def test_stories15m_q8_greedy_parity(cuda_dev, tmp_path):
     rm = O.RefModel(path, threads=1, isa=O.ISA_SCALAR)
     m = DropIn(path)
     rels, ties = greedy_parity(m.forward, m.generate, rm, prompt, 64)
+    # the reference's own SIMD path against its scalar path on the same tokens: its spread at this shape
+    # (the reference's ISA choice is process-wide: all scalar logits first, then the SIMD ones)
+    R, _, _ = rm.greedy(prompt, 64)
+    seq = list(prompt) + list(R)
+    scal = [rm.forward(seq[p], p) for p in range(len(seq) - 1)]
+    best = O.ref().ref_isa_best()
+    rs = O.RefModel(path, threads=1, isa=best)
+    isa = np.asarray([np.abs(rs.forward(seq[p], p) - scal[p]).max() / np.abs(scal[p]).max() for p in range(len(seq) - 1)])
+    rs.close()
+    O.ref().ref_isa_select(O.ISA_SCALAR)
     print(f"stories15M q8: rel logit err vs reference scalar over {len(rels)} positions: max {rels.max():.3e}, "
-          f"median {np.median(rels):.3e}, positions above 1e-5: {int((rels > 1e-5).sum())}; tie steps {ties}")
-    # the reference's same-weights tolerance (tests/test_model.c:50-53) bounds every position; an int8
-    # rounding step of one activation (the sums are ordered differently) moves single positions to ~1e-2,
-    # so the median is bounded too: most positions agree to float rounding
-    assert rels.max() < 2e-2 and np.median(rels) < 2e-3
+          f"median {np.median(rels):.3e}; the reference's ISA {best} vs its scalar: max {isa.max():.3e}, "
+          f"median {np.median(isa):.3e}; tie steps {ties}")
+    # the reference's same-weights tolerance (tests/test_model.c:50-53) bounds every position, and the GPU
+    # must stay as close to the scalar path as the reference's own SIMD path is (1.5x): an int8 rounding
+    # step of one activation (the sums are ordered differently) propagates through the KV cache
+    assert rels.max() < 2e-2 and rels.max() <= max(1e-5, 1.5 * isa.max())
+    assert np.median(rels) <= max(1e-5, 1.5 * np.median(isa))
     m.close()
 
 
