@@ -56,7 +56,7 @@ constexpr int MAXW = 4;             // head_dim / 32 (head_dim <= 128)
 constexpr int kMinAttnPos = 32;     // an attention segment spans at least this many positions
 constexpr int kAttnChunk = 4;       // positions per warp whose K/V rows are loaded together
 constexpr int kPartHead = kDecodePartHead;  // partial: (max, sum, 2 pad, acc[hd]), acc 16-byte aligned
-constexpr int kFastSegs = 4;        // segment partials the wo prologue merges with all loads in flight
+constexpr int kFastSegs = kDecodeFastSegs;  // segment partials the wo prologue merges with all loads in flight
 // named barriers: 0 = __syncthreads, kBarConsumers = all consumer warps (the producer warp never waits)
 constexpr int kBarConsumers = 1;
 // shared scratch at off_red: prologue partial sums, argmax keys, grid-barrier flag
@@ -165,6 +165,73 @@ __device__ bool grid_sync(const DecodeParams &p, uint8_t *sm, unsigned target, b
     }
     named_sync(kBarConsumers, NCT);
     return *flag != 0;
+}
+
+// ---------------------------------------------------------------- cross-rank exchange (tensor parallelism)
+// The wo / w2 row sums of a rank are partials over its column shard (src/model.c:178-186 split across the
+// ranks).  Each goes to every rank as one 64-bit word (float bits, tag) with a relaxed system-scope store:
+// single-copy atomic, so a reader that sees the tag sees the value, and no fence is needed -- a
+// system-scope release costs 3-6 us per point on B200 over NVLink, the data's own tag about one NVLink
+// latency.  After its own rows are done, each CTA polls the words of its rows (the same rows on every
+// rank: same D, same grid), adds the ranks' partials in rank order to x -- the same bits on every rank --
+// and stores x in place; the ordinary grid barrier that ends the phase then publishes x to the CTA's
+// rank.  Tags never repeat: exchange e of the step with epoch ep carries ep * xph + e + 1 (0 = empty).
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned *p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned *xch_word(const DecodeParams &p, int r, int off) {
+    return (unsigned *)(p.peers.blk[r] + off);
+}
+__device__ __forceinline__ unsigned long long *xch_slot(const DecodeParams &p, int r, int xex) {
+    return (unsigned long long *)(p.peers.blk[r] + kXchSync) + (int64_t)(xex & 1) * p.tp * p.D;
+}
+// this rank's partial of row `unit` into every rank's slot
+__device__ __forceinline__ void xch_put(const DecodeParams &p, int xex, unsigned tag, int64_t unit, float a) {
+    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(a);
+    for (int r = 0; r < p.tp; r++) st_relaxed_sys_u64(xch_slot(p, r, xex) + (int64_t)p.rank * p.D + unit, w);
+}
+// x += (p_0 + ... + p_{tp-1}) for this CTA's rows [u0, u1), the consumer threads one row each (bounded
+// polls; on expiry the error word is raised and the row keeps what has arrived)
+__device__ void xch_reduce(const DecodeParams &p, const DecodePhase &ph, unsigned tag) {
+    int64_t u0, u1;
+    split_units(ph.units, u0, u1);
+    const unsigned long long *slot = xch_slot(p, p.rank, ph.xex);
+    for (int64_t u = u0 + threadIdx.x; u < u1; u += NCT) {
+        float s = 0.0f;
+        for (int r = 0; r < p.tp; r++) {
+            const unsigned long long *q = slot + (int64_t)r * p.D + u;
+            unsigned long long w = ld_relaxed_sys_u64(q);
+            if ((unsigned)(w >> 32) != tag) {
+                const long long t0 = clock64();
+                while ((unsigned)((w = ld_relaxed_sys_u64(q)) >> 32) != tag)
+                    if (clock64() - t0 > kWaitCycles) {
+                        raise_error(p.err, kErrFlagTimeout);
+                        break;
+                    }
+            }
+            s = r == 0 ? __uint_as_float((unsigned)w) : s + __uint_as_float((unsigned)w);
+        }
+        __stcg(ph.out + u, __ldcg(ph.out + u) + s);  // residual (src/model.c:179,186)
+    }
+}
+__device__ __forceinline__ bool counter_wait_sys(const unsigned *ctr, unsigned target) {
+    const long long t0 = clock64();
+    while ((int)(ld_acquire_sys(ctr) - target) < 0)
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
 }
 
 // ---------------------------------------------------------------- phase descriptors in shared memory
@@ -558,6 +625,7 @@ __device__ void prologue(const DecodeParams &p, const DecodePhase &ph, uint8_t *
             for (int i = 0; i < 16; i++)
                 if (e0 + i < K) __stcg(p.x + e0 + i, v[i]);
         }
+
         if (norm) {
 #pragma unroll
             for (int i = 0; i < 16; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
@@ -639,7 +707,7 @@ __device__ __forceinline__ float2 epilogue_operand(const DecodeParams &p, const 
 
 template <bool KV16>
 __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhase &ph, int64_t unit, float a, float b,
-                                         float2 opnd, int pos, unsigned long long &best) {
+                                         float2 opnd, int pos, unsigned long long &best, unsigned xtag) {
     switch (ph.kind) {
     case PH_QKV: {  // rows 2u, 2u+1: one RoPE pair of q or k, or two v values
         const int64_t vr = 2 * unit;
@@ -668,11 +736,20 @@ __device__ __forceinline__ void epilogue(const DecodeParams &p, const DecodePhas
         break;
     }
     case PH_WO:
-    case PH_W2: __stcg(ph.out + unit, opnd.x + a); break;  // residual (src/model.c:179,186)
+    case PH_W2:
+        if (ph.xex < 0) __stcg(ph.out + unit, opnd.x + a);  // residual (src/model.c:179,186)
+        else xch_put(p, ph.xex, xtag, unit, a);            // a partial: the residual follows in xch_reduce
+        break;
     case PH_FFN: __stcg(ph.out + unit, __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), b)); break;  // src/ops.c:128-133
     default:  // PH_OUT
-        __stcg(ph.out + unit, a);
-        if (a == a) best = max(best, argmax_key(a, (int)unit));
+        if (p.tp == 1) {
+            __stcg(ph.out + unit, a);
+            if (a == a) best = max(best, argmax_key(a, (int)unit));
+        } else {  // the vocabulary shard's logits into every rank's full logits
+            const int64_t gu = (int64_t)p.rank * ph.units + unit;
+            for (int r = 0; r < p.tp; r++) __stcg((float *)(p.peers.blk[r] + p.xlog_off) + gu, a);
+            if (a == a) best = max(best, argmax_key(a, (int)gu));
+        }
         break;
     }
 }
@@ -724,7 +801,7 @@ __device__ __forceinline__ void unit_dot(bool two, const uint8_t *r0, int rbytes
 // their epilogues at once, their operand loads (RoPE pairs, residual x) in flight together.
 template <int DT, bool KV16>
 __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, uint64_t *full, uint64_t *empty,
-                           unsigned &gk, bool &dead, int pos, unsigned long long &best, int phi) {
+                           unsigned &gk, bool &dead, int pos, unsigned long long &best, int phi, unsigned xtag) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, grp = warp / GW, wig = warp % GW;
     const uint8_t *xq = sm + p.off_xq;
     const int2 *xds = (const int2 *)(sm + p.off_xds);
@@ -766,7 +843,7 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
         nunits += npend;
         if (lane < npend) {
             const float2 opnd = first_batch ? opre : epilogue_operand(p, ph, punit, pos);
-            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best);
+            epilogue<KV16>(p, ph, punit, pa0, pa1, opnd, pos, best, xtag);
         }
         npend = 0;
         first_batch = false;
@@ -1034,10 +1111,24 @@ __device__ void logits_argmax(const DecodeParams &p, uint8_t *sm, unsigned long 
         unsigned long long k = 0;
         for (int w = 0; w < NCW; w++) k = max(k, keys[w]);
         if (k) atomicMax(p.amax_key, k);
-        __threadfence();
+        if (p.tp > 1) __threadfence_system();  // the CTA's logits stores into the peers come first
+        else __threadfence();
         if (atomicAdd(p.amax_ctr, 1) == (int)gridDim.x - 1) {
             __threadfence();
-            const unsigned long long gmax = atomicExch(p.amax_key, 0ull);
+            unsigned long long gmax = atomicExch(p.amax_key, 0ull);
+            if (p.tp > 1) {
+                // the rank's key into every rank's table, then one system-scope arrival on every rank's
+                // key counter; every rank then takes the same maximum (and so the same token)
+                const unsigned ep = __ldcg(xch_word(p, p.rank, kXchEpoch));
+                for (int r = 0; r < p.tp; r++)
+                    __stcg((unsigned long long *)(p.peers.blk[r] + kXchKeys) + p.rank, gmax);
+                for (int r = 0; r < p.tp; r++) red_release_sys_add(xch_word(p, r, kXchKeyCtr), 1u);
+                if (!counter_wait_sys(xch_word(p, p.rank, kXchKeyCtr), (ep + 1) * (unsigned)p.tp))
+                    raise_error(p.err, kErrFlagTimeout);
+                for (int r = 0; r < p.tp; r++)
+                    gmax = max(gmax, __ldcg((const unsigned long long *)(p.peers.blk[p.rank] + kXchKeys) + r));
+                __stcg(xch_word(p, p.rank, kXchEpoch), ep + 1);  // the next step's cross-rank targets
+            }
             int bi = argmax_index(gmax);
             const float x0 = __ldcg(p.logits);
             if (x0 != x0) bi = 0;  // a NaN in slot 0 is never replaced by the reference (src/sampler.c:27-32)
@@ -1075,6 +1166,8 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
     }
     unsigned gk = 0;
     bool dead = false;
+    // tags of this step's cross-rank exchanges count from epoch * xph (every rank runs the same steps)
+    const unsigned xbase = p.tp > 1 ? __ldcg(xch_word(p, p.rank, kXchEpoch)) * (unsigned)p.xph : 0u;
     DecodePhase *dsm = (DecodePhase *)(sm + p.off_red + kRedDesc);
     desc_prefetch(p.ph, dsm);
     desc_wait();
@@ -1097,8 +1190,13 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
         if (t == 0) DTRACE_SET(i, kTrProEnd, gtime());
         unsigned long long best = 0;  // this thread's argmax key (OUT phase)
         const bool two = ph.urows == 2;
-        if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
-        else run_matvec<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i);
+        const unsigned xtag = ph.xex >= 0 ? xbase + (unsigned)ph.xex + 1u : 0u;
+        if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i, xtag);
+        else run_matvec<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i, xtag);
+        if (ph.xex >= 0 && !dead) {  // every warp's partials are out: add the ranks' partials of this CTA's rows
+            named_sync(kBarConsumers, NCT);
+            xch_reduce(p, ph, xtag);
+        }
         if (ph.kind == PH_OUT) logits_argmax(p, sm, best);
         if (ph.kind == PH_QKV) {  // the attention phase that follows reads this layer's cache
             if constexpr (KV16) attn_prefetch<__half>(p, ph, pos);

@@ -18,6 +18,7 @@ int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, voi
 
 constexpr int kDecodeHeadsPerUnit = 4;  // query heads per attention work unit
 constexpr int kDecodePartHead = 4;      // floats before acc[] in an attention segment partial
+constexpr int kDecodeFastSegs = 4;      // position segments per head the wo prologue merges with all loads in flight
 
 enum DecodePhaseKind : int { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_W2 = 4, PH_OUT = 5 };
 
@@ -34,6 +35,23 @@ struct DecodePhase {
     const float *norm_w;  // fused rmsnorm weight or null
     float *out;           // WO/W2: x (+=), FFN: h, OUT: logits
     void *kc, *vc;        // QKV / ATTN: this layer's caches [max_seq][KVl] (float or __half: kv16)
+    // tensor parallelism: exchange xex (2 x layer + {0: after wo, 1: after w2}) of the step, or -1.  The
+    // row sums are this rank's partials: they go to slot xex % 2 of every rank, tagged, and each CTA then
+    // adds the ranks' partials of its own rows to x
+    int xex;
+    int pad_[3];
+};
+
+constexpr int kDecodeMaxTp = 8;
+// per-rank exchange block (one allocation, mapped by every rank of a tensor-parallel group):
+//   [0, 256)                   sync words: u32 key counter at 16, u32 epoch at 32, u64 argmax keys
+//                              [kDecodeMaxTp] at 64
+//   [256, 256 + 16 * tp * D)   partial rows [2 slots][tp ranks][D] as 64-bit (float bits, tag) words
+//   then                       the full logits [V] floats (every rank writes its shard into every rank's)
+constexpr int kXchSync = 256;
+constexpr int kXchKeyCtr = 16, kXchEpoch = 32, kXchKeys = 64;
+struct DecodePeers {
+    uint8_t *blk[kDecodeMaxTp];  // every rank's exchange block (this rank's own at [rank])
 };
 
 struct DecodeParams {
@@ -58,6 +76,10 @@ struct DecodeParams {
     float *apart;    // attention segment partials [nkv * gsplit][maxseg][4][4 + hd]
     int maxseg;
     int kv16;  // the KV cache holds fp16 (else fp32)
+    int tp, rank;      // tensor-parallel group (tp 1: a single GPU)
+    int xph;           // cross-rank exchanges per step (2 x layers)
+    int64_t xlog_off;  // byte offset of the logits in an exchange block
+    DecodePeers peers;
     int *err;
     int nslots, slot_bytes;
     int off_bars, off_xq, off_xds, off_red;

@@ -84,6 +84,10 @@ struct qmc_model {
     int8_t *pf_aq = nullptr;
     // weight upload: pinned staging buffers (allocated on the first large upload)
     uint8_t *stage[2] = {nullptr, nullptr};
+    // tensor parallelism on the persistent path: this rank's exchange block and every rank's, mapped
+    uint8_t *xblk = nullptr;
+    uint8_t *xpeer[kDecodeMaxTp] = {};
+    int64_t xlog_off = 0;
     cudaEvent_t stage_ev[2] = {nullptr, nullptr};
 };
 
@@ -239,8 +243,10 @@ int nccl_check(ncclResult_t r, const char *what) {
 
 // ---------------------------------------------------------------- persistent decode path
 // Eligible when one GPU holds the model, every matrix is Q8_0/Q4_0 and the ring plan fits shared memory.
+int setup_exchange(qmc_model *m);
+
 bool decode_eligible(qmc_model *m, DevCtx *c) {
-    if (m->tp != 1 || m->hd > 128) return false;
+    if (m->tp > kDecodeMaxTp || m->hd > 128) return false;
     auto q = [](int dt) { return dt == QMC_Q8_0 || dt == QMC_Q4_0; };
     if (!q(m->dt_out)) return false;
     int64_t umax = split_row_bytes(m->dt_out, m->D);
@@ -253,7 +259,64 @@ bool decode_eligible(qmc_model *m, DevCtx *c) {
         umax = std::max(umax, split_row_bytes(l.dt[QMC_T_W2], m->Hl));
     }
     nbmax = std::max(nbmax, (int)std::max(nblocks(m->Dl), nblocks(m->Hl)));
-    return plan_decode(umax, nbmax, m->hd, m->NH / m->NKV, c->max_smem_optin, &m->plan);
+    if (!plan_decode(umax, nbmax, m->hd, m->NH / m->NKV, c->max_smem_optin, &m->plan)) return false;
+    // tensor parallelism: every rank maps every rank's exchange block (CUDA IPC over NVLink); where that is
+    // not possible the model keeps the per-operation graph with NCCL all-reduces.  Every rank takes the
+    // same collective steps here, so the outcome is agreed before anyone returns.
+    return m->tp == 1 || setup_exchange(m) == QMC_OK;
+}
+
+// The exchange block of this rank (zeroed: tag 0 means empty), its IPC handle all-gathered over the
+// model's NCCL communicator, and every peer's block opened.  All ranks then agree (NCCL min) on whether
+// every rank succeeded.
+int setup_exchange(qmc_model *m) {
+    const size_t bytes = (size_t)kXchSync + (size_t)16 * m->tp * m->D + (size_t)4 * m->V;
+    m->xlog_off = (int64_t)kXchSync + (int64_t)16 * m->tp * m->D;
+    int ok = 1;
+    cudaIpcMemHandle_t h{};
+    if (dalloc(m, (void **)&m->xblk, bytes) != QMC_OK || cudaMemset(m->xblk, 0, bytes + 256) != cudaSuccess ||
+        cudaIpcGetMemHandle(&h, m->xblk) != cudaSuccess)
+        ok = 0;
+    cudaGetLastError();
+    char *dh = nullptr;
+    int *dok = nullptr;
+    RC(dalloc(m, (void **)&dh, (size_t)64 * m->tp));
+    RC(dalloc(m, (void **)&dok, 4));
+    QMC_CUDA(cudaMemcpy(dh + 64 * m->rank, &h, 64, cudaMemcpyHostToDevice));
+    QMC_CUDA(cudaMemcpy(dok, &ok, 4, cudaMemcpyHostToDevice));
+    RC(nccl_check(ncclAllGather(dh + 64 * m->rank, dh, 64, ncclChar, m->comm, m->stream), "all-gather(ipc handles)"));
+    RC(nccl_check(ncclAllReduce(dok, dok, 1, ncclInt, ncclMin, m->comm, m->stream), "all-reduce(ipc ok)"));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    std::vector<char> hh((size_t)64 * m->tp);
+    QMC_CUDA(cudaMemcpy(hh.data(), dh, hh.size(), cudaMemcpyDeviceToHost));
+    QMC_CUDA(cudaMemcpy(&ok, dok, 4, cudaMemcpyDeviceToHost));
+    for (int r = 0; r < m->tp && ok; r++) {
+        if (r == m->rank) {
+            m->xpeer[r] = m->xblk;
+            continue;
+        }
+        cudaIpcMemHandle_t ph;
+        memcpy(&ph, hh.data() + 64 * r, 64);
+        void *ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, ph, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0;
+            break;
+        }
+        m->xpeer[r] = (uint8_t *)ptr;
+    }
+    QMC_CUDA(cudaMemcpy(dok, &ok, 4, cudaMemcpyHostToDevice));
+    RC(nccl_check(ncclAllReduce(dok, dok, 1, ncclInt, ncclMin, m->comm, m->stream), "all-reduce(ipc open)"));
+    QMC_CUDA(cudaStreamSynchronize(m->stream));
+    QMC_CUDA(cudaMemcpy(&ok, dok, 4, cudaMemcpyDeviceToHost));
+    if (!ok) {
+        for (int r = 0; r < m->tp; r++)
+            if (m->xpeer[r] && r != m->rank) cudaIpcCloseMemHandle(m->xpeer[r]);
+        for (int r = 0; r < m->tp; r++) m->xpeer[r] = nullptr;
+        return set_error(QMC_ECUDA, "exchange blocks could not be mapped on every rank");
+    }
+    m->logits = (float *)(m->xblk + m->xlog_off);  // every rank's shard lands in every rank's logits
+    return QMC_OK;
 }
 
 // split-row copies of every matrix (allocated once); FFN rows interleaved w1[0], w3[0], w1[1], ... so one
@@ -303,6 +366,7 @@ int repack_weights(qmc_model *m) {
 DecodePhase matrix_phase(const qmc_model *m, int grid, int kind, int dt, const uint8_t *W, int64_t units, int64_t K,
                          int urows, const float *in, const float *norm_w, float *out) {
     DecodePhase ph{};
+    ph.xex = -1;
     ph.kind = kind;
     ph.dtype = dt;
     ph.W = W;
@@ -347,18 +411,25 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
             qkv.embed = l == 0;
             qkv.kc = kcl, qkv.vc = vcl;
             DecodePhase at{};
+            at.xex = -1;
             at.kind = PH_ATTN;
             at.kc = kcl, at.vc = vcl;
             m->phases.push_back(qkv);
             m->phases.push_back(at);
-            m->phases.push_back(matrix_phase(m, c->num_sms, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x));
+            DecodePhase wo = matrix_phase(m, c->num_sms, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x);
+            DecodePhase w2 = matrix_phase(m, c->num_sms, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x);
+            wo.xex = m->tp > 1 ? 2 * l : -1;  // tensor parallelism: partial rows, exchanged across the ranks
+            w2.xex = m->tp > 1 ? 2 * l + 1 : -1;
+            m->phases.push_back(wo);
             m->phases.push_back(matrix_phase(m, c->num_sms, PH_FFN, Ly.dt[QMC_T_W1], Ly.s13, m->Hl, m->D, 2, m->x, Ly.ffn_norm, m->h));
-            m->phases.push_back(matrix_phase(m, c->num_sms, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x));
+            m->phases.push_back(w2);
         }
         m->phases.push_back(matrix_phase(m, c->num_sms, PH_OUT, m->dt_out, m->sout, m->Vl, m->D, 1, m->x, m->norm, m->logits));
         const int group = m->NH / m->NKV;
         m->gsplit = (group + kDecodeHeadsPerUnit - 1) / kDecodeHeadsPerUnit;
-        m->maxseg = std::max(1, c->num_sms / (m->NKVl * m->gsplit));
+        // at most kDecodeFastSegs segments per head: the wo prologue then merges them with every load in
+        // flight (with few KV heads per GPU, e.g. under tensor parallelism, more would take its slow path)
+        m->maxseg = std::max(1, std::min(kDecodeFastSegs, c->num_sms / (m->NKVl * m->gsplit)));
         const size_t units = (size_t)m->NKVl * m->gsplit;
         RC(dalloc(m, (void **)&m->d_phases, m->phases.size() * sizeof(DecodePhase)));
         RC(dalloc(m, (void **)&m->gbar, 64));
@@ -392,6 +463,8 @@ int launch_decode_step(qmc_model *m, DevCtx *c) {
     p.kv16 = m->kv16;
     p.err = c->err;
     p.nslots = m->plan.nslots, p.slot_bytes = m->plan.slot_bytes;
+    p.tp = m->tp, p.rank = m->rank, p.xph = 2 * m->L, p.xlog_off = m->xlog_off;
+    for (int r = 0; r < kDecodeMaxTp; r++) p.peers.blk[r] = m->xpeer[r];
     p.off_bars = m->plan.off_bars, p.off_xq = m->plan.off_xq, p.off_xds = m->plan.off_xds, p.off_red = m->plan.off_red;
     return launch_decode(p, m->plan, c->num_sms, m->stream);
 }
@@ -1012,6 +1085,8 @@ int qmc_model_free(qmc_model *m) {
     cudaSetDevice(m->dev);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (int r = 0; r < kDecodeMaxTp; r++)
+        if (m->xpeer[r] && m->xpeer[r] != m->xblk) cudaIpcCloseMemHandle(m->xpeer[r]);
     for (void *p : m->allocs) cudaFree(p);
     if (m->h_state) cudaFreeHost(m->h_state);
     if (m->h_logits) cudaFreeHost(m->h_logits);
