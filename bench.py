@@ -462,6 +462,8 @@ def gpu_arm(args, wl: dict) -> dict | None:
         out["long_context"] = long_context(qb, wl, st, e0, e1, hbm)
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args, wl)
+    if "matvec" in out:  # last, where a tail of the line keeps it: shape, dtype, fraction of the HBM peak
+        out["matvec_sweep_frac"] = {f"{r['dtype']} {r['shape']}": round(r["frac"], 3) for r in out["matvec"]}
     d.close()
     return out if d.rank == 0 else None
 

@@ -23,6 +23,8 @@
 // stays under ~112 KB of shared memory and 60 registers so the next kernel's CTA can co-reside.
 #include <stdio.h>
 
+#include <algorithm>
+
 #include "gemv.cuh"
 
 namespace qmc {
@@ -34,6 +36,11 @@ constexpr int NT = (NCW + 1) * 32;   // + one producer warp
 constexpr int CH = 4096;             // activation staging chunk (floats)
 constexpr int kStageTarget = 16 * 1024;
 constexpr int kCoResidentSmem = 112 * 1024;  // two CTAs (this kernel and the next) per SM
+// Matrices of at least this many bytes take the whole shared memory of the SM for their ring (up to
+// kDeepStages stages): streaming dominates their launch, and ~74 KB in flight per SM (the co-resident
+// footprint) cannot cover the loaded copy latency at the SM's share of the HBM bandwidth.
+constexpr int64_t kDeepBytes = 48ll << 20;
+constexpr int kDeepStages = 3 * NG;
 
 struct KParams {
     const uint8_t *W0, *W1;
@@ -546,9 +553,10 @@ int launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl, int grid_limit
     // all of group s % NG).  A slot shared by two groups breaks the parity waits: a group that runs one
     // ring lap ahead of the group before it sees the previous phase's parity as complete and reads a
     // slot whose copy has not landed.
-    int ns = (kCoResidentSmem - fixed - 256) / p.stage_bytes;
+    const bool deep = (int64_t)p.units * unit_bytes >= kDeepBytes;
+    int ns = ((deep ? (int)c->max_smem_optin : kCoResidentSmem) - fixed - 256) / p.stage_bytes;
     if (ns < NG) ns = ((int)c->max_smem_optin - fixed - 256) / p.stage_bytes;
-    ns = ns >= 2 * NG ? 2 * NG : ns >= NG ? NG : 0;
+    ns = std::min(ns, deep ? kDeepStages : 2 * NG) / NG * NG;
     if (ns == 0) return set_error(QMC_EINVAL, "gemv: K=%lld needs more shared memory than a CTA has", (long long)a.K);
     p.nstages = ns;
     p.off_bars = ns * p.stage_bytes;
