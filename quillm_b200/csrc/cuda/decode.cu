@@ -55,6 +55,7 @@ constexpr int GMAX = kDecodeHeadsPerUnit;  // query heads per attention unit (a 
 constexpr int MAXW = 4;             // head_dim / 32 (head_dim <= 128)
 constexpr int kMinAttnPos = 32;     // an attention segment spans at least this many positions
 constexpr int kAttnChunk = 4;       // positions per warp whose K/V rows are loaded together
+constexpr int kPrefetchPos = 64;    // positions of a segment prefetched into L2 before the barrier
 constexpr int kPartHead = kDecodePartHead;  // partial: (max, sum, 2 pad, acc[hd]), acc 16-byte aligned
 constexpr int kFastSegs = kDecodeFastSegs;  // segment partials the wo prologue merges with all loads in flight
 // named barriers: 0 = __syncthreads, kBarConsumers = all consumer warps (the producer warp never waits)
@@ -915,7 +916,10 @@ __device__ void attn_prefetch(const DecodeParams &p, const DecodePhase &ph, int 
     const int npos = pos + 1, nseg = attn_segments(p, pos);
     if ((int)blockIdx.x >= p.nkv * p.gsplit * nseg) return;
     const int unit = (int)blockIdx.x / nseg, seg = (int)blockIdx.x % nseg, kvh = unit / p.gsplit;
-    const int chunk = (npos + nseg - 1) / nseg, t0 = seg * chunk, t1 = min(npos, t0 + chunk);
+    // only the segment's first kPrefetchPos positions: the warps' first chunks wait on them, later chunks
+    // follow in the loop, and a whole long segment (512 positions at the end of a 2048 window) kept
+    // evict-last in L2 crowds out what the step reuses
+    const int chunk = (npos + nseg - 1) / nseg, t0 = seg * chunk, t1 = min(npos, min(t0 + chunk, t0 + kPrefetchPos));
     const int rowb = p.hd * (int)sizeof(KT), lines = (rowb + 127) / 128 + 1;  // +1: the row's last byte
     const int total = max(0, t1 - t0) * 2 * lines;
     for (int e = threadIdx.x; e < total; e += NCT) {
