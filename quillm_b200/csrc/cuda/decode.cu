@@ -255,6 +255,23 @@ __device__ __forceinline__ void desc_wait() { asm volatile("cp.async.wait_all;" 
 // warp released the slot's previous stage, so a slow warp never holds up another warp's refills.  The
 // producer never waits on a grid barrier: while the consumers sit in a barrier, an activation prologue
 // or attention, every warp's slots fill with its next stages, of the next phases too.
+// byte range of stage k of the CTA's units [u0, u1) of a phase: R whole units, or (K-split) chunk
+// k % C of unit u0 + k / C -- a unit's chunks are consecutive, each its rows' chunks back to back
+__device__ __forceinline__ void stage_span(const DecodePhase &q, int64_t u0, int64_t u1, int k, int64_t &src,
+                                           uint32_t &bytes) {
+    if (q.C == 1) {
+        const int64_t ua = u0 + (int64_t)k * q.R, ub = (int64_t)q.urows * q.rbytes;
+        src = ua * ub;
+        bytes = (uint32_t)(min((int64_t)q.R, u1 - ua) * ub);
+        return;
+    }
+    const int64_t u = u0 + k / q.C;
+    const int j = k % q.C, kbl = q.nb - (q.C - 1) * q.kb;
+    const int64_t cb = chunk_row_bytes(q.dtype, q.kb), cbl = chunk_row_bytes(q.dtype, kbl);
+    src = u * q.urows * ((q.C - 1) * cb + cbl) + (int64_t)q.urows * j * cb;
+    bytes = (uint32_t)(q.urows * (j < q.C - 1 ? cb : cbl));
+}
+
 __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uint64_t *empty) {
     const int w = threadIdx.x & 31;
     if (w >= NG) return;
@@ -262,7 +279,7 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
     // stage 0, this CTA's units [u0, u1) of it
     int i = -1, k = w;
     unsigned G = 0;
-    int64_t u0 = 0, u1 = 0, ubytes = 0;
+    int64_t u0 = 0, u1 = 0;
     int nst = 0;
     auto settle = [&]() {  // move the cursor onto the phase that holds stage G + k
         while (i < p.nph && (i < 0 || k >= nst)) {
@@ -272,8 +289,7 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
             if (i >= p.nph) break;
             const DecodePhase &q = p.ph[i];
             split_units(q.units, u0, u1);
-            ubytes = (int64_t)q.urows * q.rbytes;
-            nst = (int)((u1 - u0 + q.R - 1) / q.R);
+            nst = q.C > 1 ? (int)((u1 - u0) * q.C) : (int)((u1 - u0 + q.R - 1) / q.R);
         }
     };
     settle();
@@ -287,13 +303,14 @@ __device__ void producer(const DecodeParams &p, uint8_t *sm, uint64_t *full, uin
             const int s = (int)(g % (unsigned)p.nslots);
             if (g < (unsigned)p.nslots || mbar_test(&empty[s], ((g / p.nslots) - 1) & 1u)) {
                 const DecodePhase &q = p.ph[i];
-                const int64_t ua = u0 + (int64_t)k * q.R;
-                const uint32_t bytes = (uint32_t)(min((int64_t)q.R, u1 - ua) * ubytes);
+                int64_t src;
+                uint32_t bytes;
+                stage_span(q, u0, u1, k, src, bytes);
                 if (k == 0) DTRACE_SET(i, kTrProdFirst, gtime());
                 if (k + NG >= nst) DTRACE_MAX(i, kTrProdLast, gtime());
                 if (unsigned long long *q_ = trace_stage(p, g, 0)) *q_ = gtime();
                 mbar_arrive_tx(&full[s], bytes);
-                bulk_g2s_hint(sm + (size_t)s * p.slot_bytes, q.W + ua * ubytes, bytes, &full[s], pol);
+                bulk_g2s_hint(sm + (size_t)s * p.slot_bytes, q.W + src, bytes, &full[s], pol);
                 g_last = g, nissued++;
                 k += NG;
                 settle();
@@ -898,6 +915,71 @@ __device__ void run_matvec(bool two, const DecodeParams &p, const DecodePhase &p
     }
 }
 
+// A K-split matvec phase (rows too long for a ring slot): stage k of the CTA holds chunk j = k % C of its
+// unit u0 + k / C; warp g % NG takes global stage g as in run_matvec.  A warp dots the chunk's blocks
+// (activations from shared memory at block offset j * kb), sums over the warp and leaves the chunk's
+// row sums in shared memory; once every warp is done, each consumer thread adds one unit's chunks in
+// chunk order and runs its epilogue (operand loads of all units in flight together).
+template <int DT, bool KV16>
+__device__ void run_matvec_chunked(bool two, const DecodeParams &p, const DecodePhase &ph, uint8_t *sm, uint64_t *full,
+                                   uint64_t *empty, unsigned &gk, bool &dead, int pos, unsigned long long &best,
+                                   unsigned xtag) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, grp = warp / GW;
+    const uint8_t *xq = sm + p.off_xq;
+    const int2 *xds = (const int2 *)(sm + p.off_xds);
+    float *part = (float *)(sm + p.off_part);  // [unit][chunk][row]
+    const int C = ph.C, kb = ph.kb, UR = two ? 2 : 1;
+    int64_t u0, u1;
+    split_units(ph.units, u0, u1);
+    const int nunits = (int)(u1 - u0), nst = nunits * C;
+    const int k0 = (int)((unsigned)(grp + NG) - gk % NG) % NG;
+    for (int k = k0; k < nst; k += NG) {
+        const unsigned g = gk + (unsigned)k;
+        const int s = (int)(g % (unsigned)p.nslots);
+        if (!dead && __any_sync(0xffffffffu, !mbar_wait(&full[s], (g / p.nslots) & 1u))) {
+            dead = true;
+            if (lane == 0) raise_error(p.err, kErrMbarTimeout);
+        }
+        const int lu = k / C, j = k % C, kbj = j < C - 1 ? kb : ph.nb - (C - 1) * kb;
+        const int cbj = (int)chunk_row_bytes(DT, kbj), sbj = ((kbj * 2 + 15) / 16) * 16;
+        const uint8_t *r0 = sm + (size_t)s * p.slot_bytes, *r1 = r0 + cbj;
+        if (!dead) {
+            float a0 = 0.0f, a1 = 0.0f;
+            for (int b = lane; b < kbj; b += 32) {
+                uint32_t xr[8];
+                float rd;
+                int rs;
+                load_x(xq, xds, j * kb + b, xr, rd, rs);
+                a0 += dot_split<DT>(r0, sbj, b, xr, rd, rs);
+                if (two) a1 += dot_split<DT>(r1, sbj, b, xr, rd, rs);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+                if (two) a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+            }
+            if (lane == 0) {
+                part[(lu * C + j) * UR] = a0;
+                if (two) part[(lu * C + j) * UR + 1] = a1;
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && !dead) mbar_arrive(&empty[s]);  // a dead warp releases nothing (see run_matvec)
+    }
+    gk += (unsigned)nst;
+    named_sync(kBarConsumers, NCT);  // every chunk of the CTA's units is in part[]
+    if (dead) return;
+    for (int lu = t; lu < nunits; lu += NCT) {
+        float a0 = 0.0f, a1 = 0.0f;
+        for (int j = 0; j < C; j++) {
+            a0 += part[(lu * C + j) * UR];
+            if (two) a1 += part[(lu * C + j) * UR + 1];
+        }
+        const int64_t unit = u0 + lu;
+        epilogue<KV16>(p, ph, unit, a0, a1, epilogue_operand(p, ph, unit, pos), pos, best, xtag);
+    }
+}
+
 // ---------------------------------------------------------------- attention phase
 // Lane l holds head dimensions dim(w), w < MAXW: fp32 cache, l + 32 w (each K/V element load is one
 // coalesced 128-byte warp access); fp16 cache, the pairs 2 l + 64 i (+1), i < MAXW / 2, read as one
@@ -1195,8 +1277,14 @@ __global__ void __launch_bounds__(NT, 1) decode_step_kernel(const DecodeParams p
         unsigned long long best = 0;  // this thread's argmax key (OUT phase)
         const bool two = ph.urows == 2;
         const unsigned xtag = ph.xex >= 0 ? xbase + (unsigned)ph.xex + 1u : 0u;
-        if (ph.dtype == QMC_Q8_0) run_matvec<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i, xtag);
-        else run_matvec<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i, xtag);
+        if (ph.C > 1) {
+            if (ph.dtype == QMC_Q8_0) run_matvec_chunked<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, xtag);
+            else run_matvec_chunked<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, xtag);
+        } else if (ph.dtype == QMC_Q8_0) {
+            run_matvec<QMC_Q8_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i, xtag);
+        } else {
+            run_matvec<QMC_Q4_0, KV16>(two, p, ph, sm, full, empty, gk, dead, pos, best, i, xtag);
+        }
         if (ph.xex >= 0 && !dead) {  // every warp's partials are out: add the ranks' partials of this CTA's rows
             named_sync(kBarConsumers, NCT);
             xch_reduce(p, ph, xtag);
@@ -1225,7 +1313,46 @@ __global__ void repack_split_kernel(int dtype, const uint8_t *__restrict__ aos, 
     }
 }
 
+// one (row, block) per thread: the block's fp16 scale and quant bytes to their places in the K-split
+// layout; the scale padding of each chunk row is zeroed by the thread of the chunk's last block
+__global__ void repack_chunked_kernel(int dtype, const uint8_t *__restrict__ aos, int64_t row0, int64_t rows, int64_t K,
+                                      int kb, int urows, int per, int pos0, uint8_t *__restrict__ dst) {
+    const int64_t nb = nblocks(K);
+    const int BS = dtype == QMC_Q8_0 ? kQ8Bytes : kQ4Bytes, QB = BS - 2;
+    const int C = (int)((nb + kb - 1) / kb);
+    const int64_t kbl = nb - (int64_t)(C - 1) * kb, cb = chunk_row_bytes(dtype, kb), cbl = chunk_row_bytes(dtype, kbl);
+    const int64_t ub = (int64_t)urows * ((C - 1) * cb + cbl);  // bytes of a unit
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * nb; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / nb, b = i % nb, gr = row0 + r;
+        const int64_t u = gr / per, pos = gr % per + pos0;
+        const int j = (int)(b / kb), bj = (int)(b % kb);
+        const int64_t kbj = j < C - 1 ? kb : kbl, cbj = j < C - 1 ? cb : cbl, sbj = (kbj * 2 + 15) / 16 * 16;
+        uint8_t *d = dst + u * ub + (int64_t)urows * j * cb + pos * cbj;  // this row's chunk j
+        const uint8_t *s = aos + (r * nb + b) * BS;
+        d[2 * bj] = s[0];
+        d[2 * bj + 1] = s[1];
+        for (int k = 0; k < QB; k++) d[sbj + (int64_t)bj * QB + k] = s[2 + k];
+        if (bj == kbj - 1)
+            for (int64_t z = 2 * kbj; z < sbj; z++) d[z] = 0;
+    }
+}
+
 }  // namespace
+
+int launch_repack_chunked(int dtype, const void *aos, int64_t row0, int64_t rows, int64_t K, int kb, int urows, int per,
+                          int pos0, void *dst, cudaStream_t s) {
+    if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "repack: dtype %d is not quantized", dtype);
+    if (kb < 1 || urows < 1 || per < 1 || pos0 + per > urows || row0 < 0 || row0 % per)
+        return set_error(QMC_EINVAL, "repack: bad chunk layout");
+    if (rows <= 0) return QMC_OK;
+    const int64_t work = rows * nblocks(K);
+    const int grid = (int)std::min<int64_t>((work + 255) / 256, 65536);
+    const int kbc = (int)std::min<int64_t>(kb, nblocks(K));
+    repack_chunked_kernel<<<grid, 256, 0, s>>>(dtype, (const uint8_t *)aos, row0, rows, K, kbc, urows, per, pos0,
+                                               (uint8_t *)dst);
+    QMC_LAUNCH_CHECK();
+    return QMC_OK;
+}
 
 int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, void *dst, int64_t dst_stride,
                         cudaStream_t s) {
@@ -1245,16 +1372,35 @@ extern "C" __attribute__((visibility("default"))) int qmc_decode_trace_set(void 
 }
 #endif
 
-bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out) {
-    if (hd > 32 * MAXW) return false;
-    auto r128 = [](int64_t b) { return (b + 127) / 128 * 128; };
+namespace {
+int64_t r128(int64_t b) { return (b + 127) / 128 * 128; }
+// shared memory besides the ring: activations (or the attention merge scratch), chunk partials, the
+// reduction / descriptor area
+int64_t plan_fixed(int nb_max, int hd, int group, int64_t part_bytes, int64_t *scratch_out) {
     const int64_t act = r128((int64_t)nb_max * 32) + r128((int64_t)nb_max * 8);
     // attention merge scratch: every warp's (max, sum, acc) per query head of a unit
     const int64_t tree = r128((int64_t)NCW * std::min(std::max(group, 1), GMAX) * (hd + 2) * 4);
-    const int64_t scratch = std::max(act, tree);
+    *scratch_out = std::max(act, tree);
+    return *scratch_out + r128(part_bytes) + kRedBytes;
+}
+}  // namespace
+
+int64_t decode_slot_bytes(int nb_max, int hd, int group, size_t smem_optin, int64_t part_bytes) {
+    int64_t scratch;
+    const int64_t fixed = plan_fixed(nb_max, hd, group, part_bytes, &scratch);
+    const int ns = 3 * NG;
+    return (((int64_t)smem_optin - r128((int64_t)ns * 2 * 8) - fixed) / ns) / 128 * 128;
+}
+
+bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out,
+                 int64_t part_bytes) {
+    if (hd > 32 * MAXW) return false;
+    int64_t scratch;
+    const int64_t fixed = plan_fixed(nb_max, hd, group, part_bytes, &scratch);
+    const int64_t tree = r128((int64_t)NCW * std::min(std::max(group, 1), GMAX) * (hd + 2) * 4);
     for (int ns : {3 * NG, 2 * NG, NG}) {  // slots: a multiple of NG, so every slot belongs to one group
         const int64_t bars = r128((int64_t)ns * 2 * 8);  // full[ns], empty[ns]
-        const int64_t avail = (int64_t)smem_optin - (bars + scratch + kRedBytes);
+        const int64_t avail = (int64_t)smem_optin - (bars + fixed);
         const int64_t slot = (avail / ns) / 128 * 128;
         if (slot < max_unit_bytes) continue;
         DecodePlan d;
@@ -1264,10 +1410,11 @@ bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t s
         d.off_bars = (int)(ns * slot);
         d.off_xq = d.off_bars + (int)bars;
         d.off_xds = d.off_xq + (int)r128((int64_t)nb_max * 32);
-        d.off_red = d.off_xq + (int)scratch;
+        d.off_part = d.off_xq + (int)scratch;
+        d.off_red = d.off_part + (int)r128(part_bytes);
         d.smem = (size_t)d.off_red + kRedBytes;
-        if (d.off_xq < d.off_bars + ns * 16 || d.off_xds + (int64_t)nb_max * 8 > d.off_red ||
-            d.off_xq + tree > d.off_red || (int64_t)d.smem > (int64_t)smem_optin)
+        if (d.off_xq < d.off_bars + ns * 16 || d.off_xds + (int64_t)nb_max * 8 > d.off_part ||
+            d.off_xq + tree > d.off_part || (int64_t)d.smem > (int64_t)smem_optin)
             return false;  // regions overlap (cannot happen with the sizes above)
         *out = d;
         return true;

@@ -39,7 +39,11 @@ struct DecodePhase {
     // row sums are this rank's partials: they go to slot xex % 2 of every rank, tagged, and each CTA then
     // adds the ranks' partials of its own rows to x
     int xex;
-    int pad_[3];
+    // rows split along K (rows too long for a ring slot): C chunks of kb blocks (the last one shorter),
+    // each a stage; a unit's chunks are consecutive, a row's chunk = its scales (padded to 16 bytes) and
+    // quants.  C = 1: whole units, R per stage
+    int C, kb;
+    int pad_[1];
 };
 
 constexpr int kDecodeMaxTp = 8;
@@ -82,17 +86,37 @@ struct DecodeParams {
     DecodePeers peers;
     int *err;
     int nslots, slot_bytes;
-    int off_bars, off_xq, off_xds, off_red;
+    int off_bars, off_xq, off_xds, off_red, off_part;
 };
 
+// bytes of one row's chunk of kb blocks in the K-split layout (kb = all blocks: a split row)
+__host__ __device__ inline int64_t chunk_row_bytes(int dtype, int64_t kb) {
+    return ((kb * 2 + 15) / 16) * 16 + kb * (dtype == QMC_Q8_0 ? 32 : 16);
+}
+// K-split layout of a matrix: source row r (file layout) goes to unit r / per, position r % per + pos0,
+// of units of urows rows cut in chunks of kb blocks (kb >= ceil(K/32): the split-row layout above)
+// (row0: the global index of the first source row, so that a row range of a stacked matrix lands in its
+// own units)
+int launch_repack_chunked(int dtype, const void *aos, int64_t row0, int64_t rows, int64_t K, int kb, int urows, int per,
+                          int pos0, void *dst, cudaStream_t s);
+// bytes of a unit of urows rows split into chunks of kb blocks
+__host__ __device__ inline int64_t chunked_unit_bytes(int dtype, int64_t K, int64_t kb, int urows) {
+    const int64_t nb = (K + 31) / 32, k = kb < nb ? kb : nb, C = (nb + k - 1) / k;
+    return urows * ((C - 1) * chunk_row_bytes(dtype, k) + chunk_row_bytes(dtype, nb - (C - 1) * k));
+}
+
 struct DecodePlan {
-    int nslots = 0, slot_bytes = 0, off_bars = 0, off_xq = 0, off_xds = 0, off_red = 0;
+    int nslots = 0, slot_bytes = 0, off_bars = 0, off_xq = 0, off_xds = 0, off_red = 0, off_part = 0;
     int groups = 0;  // stage groups (consumer warps that each take every groups-th stage)
     size_t smem = 0;
 };
 // ring / shared-memory plan for the largest unit and activation length of the model; false if the
 // model does not fit (then the per-kernel path is used)
-bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out);
+// part_bytes: shared memory for the chunk partial sums of K-split phases
+bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out,
+                 int64_t part_bytes = 0);
+// the slot size of plan_decode's largest ring (what K-split chunks are cut to)
+int64_t decode_slot_bytes(int nb_max, int hd, int group, size_t smem_optin, int64_t part_bytes);
 // one CTA per SM, cooperative (all CTAs co-resident for the grid barriers)
 int launch_decode(const DecodeParams &p, const DecodePlan &plan, int grid, cudaStream_t s);
 

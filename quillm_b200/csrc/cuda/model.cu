@@ -39,6 +39,8 @@ struct Layer {
     uint8_t *sqkv = nullptr, *swo = nullptr, *s13 = nullptr, *sw2 = nullptr;  // split-row copies (persistent path)
     int dt[12];          // dtype per uploaded kind (indices QMC_T_*), -1 = missing
     unsigned dirty = 0;  // kinds (bit QMC_T_*) uploaded since the split-row copies were last refilled
+    // blocks per K-chunk of the split copies (>= the row's blocks: whole rows), chosen with the ring plan
+    int kb_qkv = 1 << 30, kb_wo = 1 << 30, kb_13 = 1 << 30, kb_w2 = 1 << 30;
 };
 }  // namespace
 
@@ -69,6 +71,8 @@ struct qmc_model {
     bool have_tok = false, have_norm = false, have_out = false;
     // persistent decode path (tp 1, quantized matrices): split-row weights, phase list, barrier state
     bool mega = false, mega_checked = false, repacked = false, out_dirty = true;
+    bool chunked = false;     // some matrix is split along K: its copy is not the tensor-core prefill's layout
+    int kb_out = 1 << 30;
     DecodePlan plan;
     std::vector<DecodePhase> phases;
     DecodePhase *d_phases = nullptr;
@@ -249,17 +253,54 @@ bool decode_eligible(qmc_model *m, DevCtx *c) {
     if (m->tp > kDecodeMaxTp || m->hd > 128) return false;
     auto q = [](int dt) { return dt == QMC_Q8_0 || dt == QMC_Q4_0; };
     if (!q(m->dt_out)) return false;
-    int64_t umax = split_row_bytes(m->dt_out, m->D);
     int nbmax = (int)nblocks(m->D);
-    for (const Layer &l : m->layers) {
+    for (const Layer &l : m->layers)
         if (!q(l.dt[QMC_T_WQ]) || !q(l.dt[QMC_T_WO]) || !q(l.dt[QMC_T_W1]) || !q(l.dt[QMC_T_W2])) return false;
-        umax = std::max(umax, 2 * split_row_bytes(l.dt[QMC_T_WQ], m->D));
-        umax = std::max(umax, 2 * split_row_bytes(l.dt[QMC_T_W1], m->D));
-        umax = std::max(umax, split_row_bytes(l.dt[QMC_T_WO], m->Dl));
-        umax = std::max(umax, split_row_bytes(l.dt[QMC_T_W2], m->Hl));
-    }
     nbmax = std::max(nbmax, (int)std::max(nblocks(m->Dl), nblocks(m->Hl)));
-    if (!plan_decode(umax, nbmax, m->hd, m->NH / m->NKV, c->max_smem_optin, &m->plan)) return false;
+    const int group = m->NH / m->NKV, grid = c->num_sms;
+    // Every matrix streams through ring slots of the largest ring (33): a unit (row / row pair) longer than
+    // a slot is split along K into chunks of the most blocks that fit.  The chunk partial sums need shared
+    // memory, which shrinks the slots: iterate until the chunking no longer grows.
+    struct Mat { int dt; int64_t K; int urows; int64_t units; int *kb; };
+    std::vector<Mat> mats;
+    for (Layer &l : m->layers) {
+        mats.push_back({l.dt[QMC_T_WQ], m->D, 2, (m->Dl + 2 * m->KVl) / 2, &l.kb_qkv});
+        mats.push_back({l.dt[QMC_T_WO], m->Dl, 1, m->D, &l.kb_wo});
+        mats.push_back({l.dt[QMC_T_W1], m->D, 2, m->Hl, &l.kb_13});
+        mats.push_back({l.dt[QMC_T_W2], m->Hl, 1, m->D, &l.kb_w2});
+    }
+    mats.push_back({m->dt_out, m->D, 1, m->Vl, &m->kb_out});
+    // whole rows when the largest unit fits some ring (33, 22 or 11 slots): the plan of every model that
+    // needs no split, and the layout the tensor-core prefill reads
+    int64_t umax = 0;
+    for (const Mat &x : mats) umax = std::max(umax, (int64_t)x.urows * split_row_bytes(x.dt, x.K));
+    m->chunked = false;
+    if (plan_decode(umax, nbmax, m->hd, group, c->max_smem_optin, &m->plan))
+        return m->tp == 1 || setup_exchange(m) == QMC_OK;
+    int64_t part = 0, stage_max = 0;
+    for (int it = 0; it < 4; it++) {  // otherwise split every unit longer than a slot of the 33-slot ring
+        const int64_t slot = decode_slot_bytes(nbmax, m->hd, group, c->max_smem_optin, part);
+        int64_t need = 0;
+        stage_max = 0;
+        m->chunked = false;
+        for (const Mat &x : mats) {
+            const int64_t nb = nblocks(x.K);
+            int64_t kb = nb;
+            if ((int64_t)x.urows * split_row_bytes(x.dt, x.K) > slot) {
+                kb = 0;
+                while (kb + 1 < nb && (int64_t)x.urows * chunk_row_bytes(x.dt, kb + 1) <= slot) kb++;
+                if (kb < 1) return false;
+                m->chunked = true;
+                const int64_t C = (nb + kb - 1) / kb;
+                need = std::max(need, (x.units + grid - 1) / grid * C * x.urows * 4);
+            }
+            *x.kb = (int)kb;
+            stage_max = std::max(stage_max, (int64_t)x.urows * chunk_row_bytes(x.dt, kb));
+        }
+        if (need <= part) break;
+        part = need;
+    }
+    if (!plan_decode(stage_max, nbmax, m->hd, group, c->max_smem_optin, &m->plan, part)) return false;
     // tensor parallelism: every rank maps every rank's exchange block (CUDA IPC over NVLink); where that is
     // not possible the model keeps the per-operation graph with NCCL all-reduces.  Every rank takes the
     // same collective steps here, so the outcome is agreed before anyone returns.
@@ -320,43 +361,48 @@ int setup_exchange(qmc_model *m) {
 }
 
 // split-row copies of every matrix (allocated once); FFN rows interleaved w1[0], w3[0], w1[1], ... so one
-// copy streams both rows of a SwiGLU unit.  Only the kinds uploaded since the last refill are repacked,
-// layer by layer, and each layer's file-layout copies are released right after: the persistent path
-// reads only the split-row copies (and prefill the same), so the model holds its weights once.  A later
-// upload of one tensor allocates its file-layout buffer again, and only its rows are repacked.  The
-// output matrix keeps its file-layout copy too (the batched prompt forward's final GEMV reads it).
+// copy streams both rows of a SwiGLU unit; rows longer than a ring slot split along K (decode.cuh).  Only
+// the kinds uploaded since the last refill are repacked, layer by layer, and each layer's file-layout
+// copies are released right after: the persistent path reads only the split-row copies (and the
+// tensor-core prefill the same), so the model holds its weights once.  A later upload of one tensor
+// allocates its file-layout buffer again, and only its rows are repacked.  Models with K-split matrices
+// keep the file-layout copies (their batched prompt forward runs the CUDA-core contraction on them), and
+// the output matrix keeps its copy too (the batched prompt forward's final GEMV reads it).
 int repack_weights(qmc_model *m) {
     cudaStream_t s = m->stream;
     for (Layer &l : m->layers) {
         const int dq = l.dt[QMC_T_WQ], dw = l.dt[QMC_T_WO], d1 = l.dt[QMC_T_W1], d2 = l.dt[QMC_T_W2];
-        const int64_t rq = split_row_bytes(dq, m->D), ro = split_row_bytes(dw, m->Dl), r1 = split_row_bytes(d1, m->D),
-                      r2 = split_row_bytes(d2, m->Hl);
         const int64_t nq = m->Dl + 2 * m->KVl, aq = rbytes(dq, m->D);
-        if (!l.sqkv && (dalloc(m, (void **)&l.sqkv, (size_t)(nq * rq)) || dalloc(m, (void **)&l.swo, (size_t)(m->D * ro)) ||
-                        dalloc(m, (void **)&l.s13, (size_t)(2 * m->Hl * r1)) || dalloc(m, (void **)&l.sw2, (size_t)(m->D * r2))))
+        const int64_t uq = chunked_unit_bytes(dq, m->D, l.kb_qkv, 2), uo = chunked_unit_bytes(dw, m->Dl, l.kb_wo, 1),
+                      u13 = chunked_unit_bytes(d1, m->D, l.kb_13, 2), u2 = chunked_unit_bytes(d2, m->Hl, l.kb_w2, 1);
+        if (!l.sqkv && (dalloc(m, (void **)&l.sqkv, (size_t)(nq / 2 * uq)) || dalloc(m, (void **)&l.swo, (size_t)(m->D * uo)) ||
+                        dalloc(m, (void **)&l.s13, (size_t)(m->Hl * u13)) || dalloc(m, (void **)&l.sw2, (size_t)(m->D * u2))))
             return QMC_ENOMEM;
         const unsigned d = l.dirty;
         if (!d) continue;
-        // wq | wk | wv row ranges of the stacked matrix
+        // wq | wk | wv row ranges of the stacked matrix (pairs of consecutive rows are units)
         const int64_t q0[3] = {0, m->Dl, m->Dl + m->KVl}, qn[3] = {m->Dl, m->KVl, m->KVl};
         const int qk[3] = {QMC_T_WQ, QMC_T_WK, QMC_T_WV};
         for (int j = 0; j < 3; j++)
-            if (d & (1u << qk[j])) RC(launch_repack_split(dq, l.wqkv + q0[j] * aq, qn[j], m->D, l.sqkv + q0[j] * rq, rq, s));
-        if (d & (1u << QMC_T_WO)) RC(launch_repack_split(dw, l.wo, m->D, m->Dl, l.swo, ro, s));
-        if (d & (1u << QMC_T_W1)) RC(launch_repack_split(d1, l.w1, m->Hl, m->D, l.s13, 2 * r1, s));
-        if (d & (1u << QMC_T_W3)) RC(launch_repack_split(d1, l.w3, m->Hl, m->D, l.s13 + r1, 2 * r1, s));
-        if (d & (1u << QMC_T_W2)) RC(launch_repack_split(d2, l.w2, m->D, m->Hl, l.sw2, r2, s));
+            if (d & (1u << qk[j]))
+                RC(launch_repack_chunked(dq, l.wqkv + q0[j] * aq, q0[j], qn[j], m->D, l.kb_qkv, 2, 2, 0, l.sqkv, s));
+        if (d & (1u << QMC_T_WO)) RC(launch_repack_chunked(dw, l.wo, 0, m->D, m->Dl, l.kb_wo, 1, 1, 0, l.swo, s));
+        if (d & (1u << QMC_T_W1)) RC(launch_repack_chunked(d1, l.w1, 0, m->Hl, m->D, l.kb_13, 2, 1, 0, l.s13, s));
+        if (d & (1u << QMC_T_W3)) RC(launch_repack_chunked(d1, l.w3, 0, m->Hl, m->D, l.kb_13, 2, 1, 1, l.s13, s));
+        if (d & (1u << QMC_T_W2)) RC(launch_repack_chunked(d2, l.w2, 0, m->D, m->Hl, l.kb_w2, 1, 1, 0, l.sw2, s));
         QMC_CUDA(cudaStreamSynchronize(s));
-        RC(dfree(m, &l.wqkv));
-        RC(dfree(m, &l.wo));
-        RC(dfree(m, &l.w1));
-        RC(dfree(m, &l.w3));
-        RC(dfree(m, &l.w2));
+        if (!m->chunked) {
+            RC(dfree(m, &l.wqkv));
+            RC(dfree(m, &l.wo));
+            RC(dfree(m, &l.w1));
+            RC(dfree(m, &l.w3));
+            RC(dfree(m, &l.w2));
+        }
         l.dirty = 0;
     }
-    const int64_t rout = split_row_bytes(m->dt_out, m->D);
-    if (!m->sout && dalloc(m, (void **)&m->sout, (size_t)(m->Vl * rout))) return QMC_ENOMEM;
-    if (m->out_dirty) RC(launch_repack_split(m->dt_out, m->out, m->Vl, m->D, m->sout, rout, s));
+    const int64_t uout = chunked_unit_bytes(m->dt_out, m->D, m->kb_out, 1);
+    if (!m->sout && dalloc(m, (void **)&m->sout, (size_t)(m->Vl * uout))) return QMC_ENOMEM;
+    if (m->out_dirty) RC(launch_repack_chunked(m->dt_out, m->out, 0, m->Vl, m->D, m->kb_out, 1, 1, 0, m->sout, s));
     m->out_dirty = false;
     QMC_CUDA(cudaStreamSynchronize(s));
     m->repacked = true;
@@ -364,9 +410,11 @@ int repack_weights(qmc_model *m) {
 }
 
 DecodePhase matrix_phase(const qmc_model *m, int grid, int kind, int dt, const uint8_t *W, int64_t units, int64_t K,
-                         int urows, const float *in, const float *norm_w, float *out) {
+                         int urows, const float *in, const float *norm_w, float *out, int kb) {
     DecodePhase ph{};
     ph.xex = -1;
+    ph.kb = (int)std::min<int64_t>(kb, nblocks(K));
+    ph.C = (int)((nblocks(K) + ph.kb - 1) / ph.kb);
     ph.kind = kind;
     ph.dtype = dt;
     ph.W = W;
@@ -391,6 +439,7 @@ DecodePhase matrix_phase(const qmc_model *m, int grid, int kind, int dt, const u
             ph.R = (int)r;
             break;
         }
+    if (ph.C > 1) ph.R = 1;  // a stage is one chunk of one unit
     ph.in = in;
     ph.norm_w = norm_w;
     ph.out = out;
@@ -407,7 +456,7 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
             Layer &Ly = m->layers[l];
             void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
             DecodePhase qkv = matrix_phase(m, c->num_sms, PH_QKV, Ly.dt[QMC_T_WQ], Ly.sqkv, (m->Dl + 2 * m->KVl) / 2, m->D, 2, m->x,
-                                           Ly.attn_norm, nullptr);
+                                           Ly.attn_norm, nullptr, Ly.kb_qkv);
             qkv.embed = l == 0;
             qkv.kc = kcl, qkv.vc = vcl;
             DecodePhase at{};
@@ -416,15 +465,15 @@ int prepare_decode(qmc_model *m, DevCtx *c) {
             at.kc = kcl, at.vc = vcl;
             m->phases.push_back(qkv);
             m->phases.push_back(at);
-            DecodePhase wo = matrix_phase(m, c->num_sms, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x);
-            DecodePhase w2 = matrix_phase(m, c->num_sms, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x);
+            DecodePhase wo = matrix_phase(m, c->num_sms, PH_WO, Ly.dt[QMC_T_WO], Ly.swo, m->D, m->Dl, 1, m->xb, nullptr, m->x, Ly.kb_wo);
+            DecodePhase w2 = matrix_phase(m, c->num_sms, PH_W2, Ly.dt[QMC_T_W2], Ly.sw2, m->D, m->Hl, 1, m->h, nullptr, m->x, Ly.kb_w2);
             wo.xex = m->tp > 1 ? 2 * l : -1;  // tensor parallelism: partial rows, exchanged across the ranks
             w2.xex = m->tp > 1 ? 2 * l + 1 : -1;
             m->phases.push_back(wo);
-            m->phases.push_back(matrix_phase(m, c->num_sms, PH_FFN, Ly.dt[QMC_T_W1], Ly.s13, m->Hl, m->D, 2, m->x, Ly.ffn_norm, m->h));
+            m->phases.push_back(matrix_phase(m, c->num_sms, PH_FFN, Ly.dt[QMC_T_W1], Ly.s13, m->Hl, m->D, 2, m->x, Ly.ffn_norm, m->h, Ly.kb_13));
             m->phases.push_back(w2);
         }
-        m->phases.push_back(matrix_phase(m, c->num_sms, PH_OUT, m->dt_out, m->sout, m->Vl, m->D, 1, m->x, m->norm, m->logits));
+        m->phases.push_back(matrix_phase(m, c->num_sms, PH_OUT, m->dt_out, m->sout, m->Vl, m->D, 1, m->x, m->norm, m->logits, m->kb_out));
         const int group = m->NH / m->NKV;
         m->gsplit = (group + kDecodeHeadsPerUnit - 1) / kDecodeHeadsPerUnit;
         // at most kDecodeFastSegs segments per head: the wo prologue then merges them with every load in
@@ -462,7 +511,7 @@ int launch_decode_step(qmc_model *m, DevCtx *c) {
     p.apart = m->apart, p.maxseg = m->maxseg;
     p.kv16 = m->kv16;
     p.err = c->err;
-    p.nslots = m->plan.nslots, p.slot_bytes = m->plan.slot_bytes;
+    p.nslots = m->plan.nslots, p.slot_bytes = m->plan.slot_bytes, p.off_part = m->plan.off_part;
     p.tp = m->tp, p.rank = m->rank, p.xph = 2 * m->L, p.xlog_off = m->xlog_off;
     for (int r = 0; r < kDecodeMaxTp; r++) p.peers.blk[r] = m->xpeer[r];
     p.off_bars = m->plan.off_bars, p.off_xq = m->plan.off_xq, p.off_xds = m->plan.off_xds, p.off_red = m->plan.off_red;
@@ -880,7 +929,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     DevCtx *c = ctx();
     if (!complete(m)) return set_error(QMC_ESTATE, "prefill: model incomplete");
     RC(prepare_decode(m, c));  // quantized single-GPU models: the split-row copies the tensor cores read
-    const bool tc = m->mega;
+    const bool tc = m->mega && !m->chunked;  // the tensor-core contraction reads whole split rows
     const int D = m->D, Dq = m->Dl, KVl = m->KVl, H = m->Hl, NQKV = Dq + 2 * KVl;
     const float eps = m->cfg.norm_eps;
     QMC_CUDA(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
