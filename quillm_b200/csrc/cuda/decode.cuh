@@ -115,7 +115,7 @@ struct DecodePlan {
 // part_bytes: shared memory for the chunk partial sums of K-split phases
 bool plan_decode(int64_t max_unit_bytes, int nb_max, int hd, int group, size_t smem_optin, DecodePlan *out,
                  int64_t part_bytes = 0);
-// the slot size of plan_decode's largest ring (what K-split chunks are cut to)
+// the slot size of plan_decode's 22-slot ring (what K-split chunks are cut to)
 int64_t decode_slot_bytes(int nb_max, int hd, int group, size_t smem_optin, int64_t part_bytes);
 // one CTA per SM, cooperative (all CTAs co-resident for the grid barriers)
 int launch_decode(const DecodeParams &p, const DecodePlan &plan, int grid, cudaStream_t s);

@@ -258,8 +258,8 @@ bool decode_eligible(qmc_model *m, DevCtx *c) {
         if (!q(l.dt[QMC_T_WQ]) || !q(l.dt[QMC_T_WO]) || !q(l.dt[QMC_T_W1]) || !q(l.dt[QMC_T_W2])) return false;
     nbmax = std::max(nbmax, (int)std::max(nblocks(m->Dl), nblocks(m->Hl)));
     const int group = m->NH / m->NKV, grid = c->num_sms;
-    // Every matrix streams through ring slots of the largest ring (33): a unit (row / row pair) longer than
-    // a slot is split along K into chunks of the most blocks that fit.  The chunk partial sums need shared
+    // Every matrix streams through ring slots: a unit (row / row pair) longer than a slot is split along K
+    // into chunks of the most blocks that fit.  The chunk partial sums need shared
     // memory, which shrinks the slots: iterate until the chunking no longer grows.
     struct Mat { int dt; int64_t K; int urows; int64_t units; int *kb; };
     std::vector<Mat> mats;
@@ -278,7 +278,7 @@ bool decode_eligible(qmc_model *m, DevCtx *c) {
     if (plan_decode(umax, nbmax, m->hd, group, c->max_smem_optin, &m->plan))
         return m->tp == 1 || setup_exchange(m) == QMC_OK;
     int64_t part = 0, stage_max = 0;
-    for (int it = 0; it < 4; it++) {  // otherwise split every unit longer than a slot of the 33-slot ring
+    for (int it = 0; it < 4; it++) {  // otherwise split every unit longer than a slot of the 22-slot ring
         const int64_t slot = decode_slot_bytes(nbmax, m->hd, group, c->max_smem_optin, part);
         int64_t need = 0;
         stage_max = 0;
