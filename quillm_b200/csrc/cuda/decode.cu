@@ -43,7 +43,7 @@
 namespace qmc {
 namespace {
 
-constexpr int NCW = 11;             // consumer warps (12 warps in all: at most 3 per SM sub-partition, so
+constexpr int NCW = kDecodeWarps;   // consumer warps (12 warps in all: at most 3 per SM sub-partition, so
                                     // each thread may hold 168 registers; with 13 warps the cap is 128 and
                                     // the whole-step kernel spills)
 constexpr int NG = NCW, GW = 1;     // stage groups x warps per group: each warp consumes its own stages

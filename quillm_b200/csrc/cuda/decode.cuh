@@ -17,6 +17,7 @@ int launch_repack_split(int dtype, const void *aos, int64_t rows, int64_t K, voi
                         cudaStream_t s);
 
 constexpr int kDecodeHeadsPerUnit = 4;  // query heads per attention work unit
+constexpr int kDecodeWarps = 11;        // consumer warps per CTA (a ring has a multiple of this many slots)
 constexpr int kDecodePartHead = 4;      // floats before acc[] in an attention segment partial
 constexpr int kDecodeFastSegs = 4;      // position segments per head the wo prologue merges with all loads in flight
 

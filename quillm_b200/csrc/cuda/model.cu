@@ -37,6 +37,9 @@ struct Layer {
     float *attn_norm = nullptr, *ffn_norm = nullptr;
     uint8_t *wqkv = nullptr, *wo = nullptr, *w1 = nullptr, *w3 = nullptr, *w2 = nullptr;
     uint8_t *sqkv = nullptr, *swo = nullptr, *s13 = nullptr, *sw2 = nullptr;  // split-row copies (persistent path)
+    // whole-row split copies for the tensor-core prefill: the same buffers as above, or, for a matrix
+    // split along K, a second copy with whole rows
+    uint8_t *pqkv = nullptr, *pwo = nullptr, *p13 = nullptr, *pw2 = nullptr;
     int dt[12];          // dtype per uploaded kind (indices QMC_T_*), -1 = missing
     unsigned dirty = 0;  // kinds (bit QMC_T_*) uploaded since the split-row copies were last refilled
     // blocks per K-chunk of the split copies (>= the row's blocks: whole rows), chosen with the ring plan
@@ -270,12 +273,13 @@ bool decode_eligible(qmc_model *m, DevCtx *c) {
         mats.push_back({l.dt[QMC_T_W2], m->Hl, 1, m->D, &l.kb_w2});
     }
     mats.push_back({m->dt_out, m->D, 1, m->Vl, &m->kb_out});
-    // whole rows when the largest unit fits some ring (33, 22 or 11 slots): the plan of every model that
-    // needs no split, and the layout the tensor-core prefill reads
+    // whole rows when the largest unit fits a ring with at least two slots per consumer warp (33 or 22
+    // slots): with one slot per warp (11) a warp's next stage cannot be in flight while it computes, and
+    // K-chunks cut to the 22-slot ring decode faster (Llama-7B-shaped Q8_0: 407.9 against 386.1 tok/s)
     int64_t umax = 0;
     for (const Mat &x : mats) umax = std::max(umax, (int64_t)x.urows * split_row_bytes(x.dt, x.K));
     m->chunked = false;
-    if (plan_decode(umax, nbmax, m->hd, group, c->max_smem_optin, &m->plan))
+    if (plan_decode(umax, nbmax, m->hd, group, c->max_smem_optin, &m->plan) && m->plan.nslots >= 2 * kDecodeWarps)
         return m->tp == 1 || setup_exchange(m) == QMC_OK;
     int64_t part = 0, stage_max = 0;
     for (int it = 0; it < 4; it++) {  // otherwise split every unit longer than a slot of the 22-slot ring
@@ -365,9 +369,9 @@ int setup_exchange(qmc_model *m) {
 // the kinds uploaded since the last refill are repacked, layer by layer, and each layer's file-layout
 // copies are released right after: the persistent path reads only the split-row copies (and the
 // tensor-core prefill the same), so the model holds its weights once.  A later upload of one tensor
-// allocates its file-layout buffer again, and only its rows are repacked.  Models with K-split matrices
-// keep the file-layout copies (their batched prompt forward runs the CUDA-core contraction on them), and
-// the output matrix keeps its copy too (the batched prompt forward's final GEMV reads it).
+// allocates its file-layout buffer again, and only its rows are repacked.  A matrix split along K for
+// decode also keeps a whole-row copy for the tensor-core prefill (two copies), and the output matrix
+// keeps its file-layout copy (the batched prompt forward's final GEMV reads it).
 int repack_weights(qmc_model *m) {
     cudaStream_t s = m->stream;
     for (Layer &l : m->layers) {
@@ -378,26 +382,47 @@ int repack_weights(qmc_model *m) {
         if (!l.sqkv && (dalloc(m, (void **)&l.sqkv, (size_t)(nq / 2 * uq)) || dalloc(m, (void **)&l.swo, (size_t)(m->D * uo)) ||
                         dalloc(m, (void **)&l.s13, (size_t)(m->Hl * u13)) || dalloc(m, (void **)&l.sw2, (size_t)(m->D * u2))))
             return QMC_ENOMEM;
+        // the tensor-core prefill's whole-row copy of a K-split matrix (the same buffer otherwise)
+        const int64_t nbq = nblocks(m->D), nbo = nblocks(m->Dl), nbh = nblocks(m->Hl);
+        auto whole = [&](uint8_t **pc, uint8_t *sc, bool split, size_t bytes) -> int {
+            if (!split) {
+                *pc = sc;
+                return QMC_OK;
+            }
+            return *pc ? QMC_OK : dalloc(m, (void **)pc, bytes);
+        };
+        RC(whole(&l.pqkv, l.sqkv, l.kb_qkv < nbq, (size_t)(nq * split_row_bytes(dq, m->D))));
+        RC(whole(&l.pwo, l.swo, l.kb_wo < nbo, (size_t)(m->D * split_row_bytes(dw, m->Dl))));
+        RC(whole(&l.p13, l.s13, l.kb_13 < nbq, (size_t)(2 * m->Hl * split_row_bytes(d1, m->D))));
+        RC(whole(&l.pw2, l.sw2, l.kb_w2 < nbh, (size_t)(m->D * split_row_bytes(d2, m->Hl))));
         const unsigned d = l.dirty;
         if (!d) continue;
         // wq | wk | wv row ranges of the stacked matrix (pairs of consecutive rows are units)
         const int64_t q0[3] = {0, m->Dl, m->Dl + m->KVl}, qn[3] = {m->Dl, m->KVl, m->KVl};
         const int qk[3] = {QMC_T_WQ, QMC_T_WK, QMC_T_WV};
-        for (int j = 0; j < 3; j++)
-            if (d & (1u << qk[j]))
-                RC(launch_repack_chunked(dq, l.wqkv + q0[j] * aq, q0[j], qn[j], m->D, l.kb_qkv, 2, 2, 0, l.sqkv, s));
-        if (d & (1u << QMC_T_WO)) RC(launch_repack_chunked(dw, l.wo, 0, m->D, m->Dl, l.kb_wo, 1, 1, 0, l.swo, s));
-        if (d & (1u << QMC_T_W1)) RC(launch_repack_chunked(d1, l.w1, 0, m->Hl, m->D, l.kb_13, 2, 1, 0, l.s13, s));
-        if (d & (1u << QMC_T_W3)) RC(launch_repack_chunked(d1, l.w3, 0, m->Hl, m->D, l.kb_13, 2, 1, 1, l.s13, s));
-        if (d & (1u << QMC_T_W2)) RC(launch_repack_chunked(d2, l.w2, 0, m->D, m->Hl, l.kb_w2, 1, 1, 0, l.sw2, s));
-        QMC_CUDA(cudaStreamSynchronize(s));
-        if (!m->chunked) {
-            RC(dfree(m, &l.wqkv));
-            RC(dfree(m, &l.wo));
-            RC(dfree(m, &l.w1));
-            RC(dfree(m, &l.w3));
-            RC(dfree(m, &l.w2));
+        // each kind into the decode copy and, when that one is split along K, into the whole-row copy too
+        const int big = 1 << 30;
+        for (int pass = 0; pass < 2; pass++) {
+            const bool w = pass == 1;
+            for (int j = 0; j < 3; j++)
+                if ((d & (1u << qk[j])) && (!w || l.pqkv != l.sqkv))
+                    RC(launch_repack_chunked(dq, l.wqkv + q0[j] * aq, q0[j], qn[j], m->D, w ? big : l.kb_qkv, 2, 2, 0,
+                                             w ? l.pqkv : l.sqkv, s));
+            if ((d & (1u << QMC_T_WO)) && (!w || l.pwo != l.swo))
+                RC(launch_repack_chunked(dw, l.wo, 0, m->D, m->Dl, w ? big : l.kb_wo, 1, 1, 0, w ? l.pwo : l.swo, s));
+            if ((d & (1u << QMC_T_W1)) && (!w || l.p13 != l.s13))
+                RC(launch_repack_chunked(d1, l.w1, 0, m->Hl, m->D, w ? big : l.kb_13, 2, 1, 0, w ? l.p13 : l.s13, s));
+            if ((d & (1u << QMC_T_W3)) && (!w || l.p13 != l.s13))
+                RC(launch_repack_chunked(d1, l.w3, 0, m->Hl, m->D, w ? big : l.kb_13, 2, 1, 1, w ? l.p13 : l.s13, s));
+            if ((d & (1u << QMC_T_W2)) && (!w || l.pw2 != l.sw2))
+                RC(launch_repack_chunked(d2, l.w2, 0, m->D, m->Hl, w ? big : l.kb_w2, 1, 1, 0, w ? l.pw2 : l.sw2, s));
         }
+        QMC_CUDA(cudaStreamSynchronize(s));
+        RC(dfree(m, &l.wqkv));
+        RC(dfree(m, &l.wo));
+        RC(dfree(m, &l.w1));
+        RC(dfree(m, &l.w3));
+        RC(dfree(m, &l.w2));
         l.dirty = 0;
     }
     const int64_t uout = chunked_unit_bytes(m->dt_out, m->D, m->kb_out, 1);
@@ -929,7 +954,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     DevCtx *c = ctx();
     if (!complete(m)) return set_error(QMC_ESTATE, "prefill: model incomplete");
     RC(prepare_decode(m, c));  // quantized single-GPU models: the split-row copies the tensor cores read
-    const bool tc = m->mega && !m->chunked;  // the tensor-core contraction reads whole split rows
+    const bool tc = m->mega;  // the tensor-core contraction reads the whole-row split copies
     const int D = m->D, Dq = m->Dl, KVl = m->KVl, H = m->Hl, NQKV = Dq + 2 * KVl;
     const float eps = m->cfg.norm_eps;
     QMC_CUDA(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
@@ -939,7 +964,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
         void *kcl = kv_layer(m, m->kc, l), *vcl = kv_layer(m, m->vc, l);
         if (tc) {  // the previous layer's w2 residual is added here, fused with the norm
             RC(prefill_norm_quant(m, l > 0 ? m->pf_c : nullptr, Ly.attn_norm, n));
-            RC(prefill_proj_tc(m, Ly.dt[QMC_T_WQ], Ly.sqkv, nullptr, n, NQKV, D, m->pf_qkv, nullptr));
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_WQ], Ly.pqkv, nullptr, n, NQKV, D, m->pf_qkv, nullptr));
         } else {
             RC(launch_rmsnorm_rows(m->pf_x, Ly.attn_norm, m->pf_xn, n, D, eps, s));
             RC(prefill_proj(m, Ly.dt[QMC_T_WQ], Ly.wqkv, m->pf_xn, n, NQKV, D, m->pf_qkv));
@@ -947,11 +972,11 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
         RC(launch_rope_kv_rows(m->pf_qkv, n, Dq, KVl, m->hd, pos0, m->rope, kcl, vcl, m->kv16 != 0, s));
         RC(launch_attn_prefill(m->pf_qkv, n, NQKV, m->NHl, m->NH / m->NKV, m->hd, KVl, pos0, 1.0f / sqrtf((float)m->hd), kcl,
                                vcl, m->kv16 != 0, m->pf_att, s));
-        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WO], Ly.swo, m->pf_att, n, D, Dq, m->pf_c, nullptr));
+        if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WO], Ly.pwo, m->pf_att, n, D, Dq, m->pf_c, nullptr));
         else RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
         if (tc) {  // wo residual fused with the norm
             RC(prefill_norm_quant(m, m->pf_c, Ly.ffn_norm, n));
-            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.s13, nullptr, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.p13, nullptr, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
         } else {
             RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
             RC(launch_rmsnorm_rows(m->pf_x, Ly.ffn_norm, m->pf_xn, n, D, eps, s));
@@ -960,7 +985,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
         }
         if (tc) {  // SwiGLU straight into the w2 contraction's activation blocks
             RC(launch_swiglu_quant_rows(m->pf_h, m->pf_h3, n, H, m->pf_aq, m->pf_ad, m->pf_adT, matmul_tc_scale_ld(n), s));
-            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W2], Ly.sw2, nullptr, n, D, H, m->pf_c, nullptr));
+            RC(prefill_proj_tc(m, Ly.dt[QMC_T_W2], Ly.pw2, nullptr, n, D, H, m->pf_c, nullptr));
         } else {
             RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
             RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
