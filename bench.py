@@ -479,19 +479,27 @@ def tp_parity(qb, wl: dict, model, prompt, d) -> dict | None:
     top-2 gap is within twice the observed difference (the summation order differs across the ranks'
     shards, as it does between the reference's own SIMD paths).  Rank 0 returns the summary."""
     P, T = len(prompt), TP_PARITY_TOKENS
-    seq, ref = None, None
-    if d.rank == 0:
-        m1 = qb.Model(dict(wl["cfg"]))
-        m1.synthesize(wl["dtype"], wl["seed"], STD)
-        gen = [int(t) for t in m1.generate(prompt, T)]
-        seq = [int(t) for t in prompt] + gen
-        ref = []
-        for p in range(P - 1, P + T - 1):  # the cache holds the sequence: the same K/V are rewritten
-            lg = np.zeros(wl["cfg"]["vocab_size"], np.float32)
-            m1.forward(seq[p], p, lg)
-            ref.append(lg)
-        m1.close()
+    seq, ref, why = None, None, None
+    if d.rank == 0:  # every rank reaches the broadcast below, with None when the TP=1 run failed
+        m1 = None
+        try:
+            m1 = qb.Model(dict(wl["cfg"]))
+            m1.synthesize(wl["dtype"], wl["seed"], STD)
+            gen = [int(t) for t in m1.generate(prompt, T)]
+            ref = []
+            for p in range(P - 1, P + T - 1):  # the cache holds the sequence: the same K/V are rewritten
+                lg = np.zeros(wl["cfg"]["vocab_size"], np.float32)
+                m1.forward(([int(t) for t in prompt] + gen)[p], p, lg)
+                ref.append(lg)
+            seq = [int(t) for t in prompt] + gen
+        except Exception as e:  # e.g. the whole model does not fit beside this rank's shard
+            why = str(e)
+        finally:
+            if m1 is not None:
+                m1.close()
     seq = d.broadcast_object(seq)
+    if seq is None:
+        return {"reference": "the same model on 1 GPU (TP=1)", "unavailable": why} if d.rank == 0 else None
     model.generate(seq[:P], 1)  # the prompt's cache slots, device-resident
     rels, ties, disagree = [], 0, 0
     for j, p in enumerate(range(P - 1, P + T - 1)):

@@ -1315,25 +1315,65 @@ __global__ void repack_split_kernel(int dtype, const uint8_t *__restrict__ aos, 
 
 // one (row, block) per thread: the block's fp16 scale and quant bytes to their places in the K-split
 // layout; the scale padding of each chunk row is zeroed by the thread of the chunk's last block
+// where block b of global row gr lives in a K-split layout (chunks of kb blocks, units of urows rows, row
+// gr at unit gr / per, position gr % per + pos0): its scale at *sc, its quants at *qu; zpad/zend: the
+// scale padding of its chunk row, which the chunk's last block owns (empty for the others)
+struct ChunkLayout {
+    int dtype, urows, per, pos0;
+    int64_t nb, kb, C, kbl, cb, cbl, ub;
+    __device__ ChunkLayout(int dt, int64_t K, int kb_, int ur, int pr, int p0) : dtype(dt), urows(ur), per(pr), pos0(p0) {
+        nb = nblocks(K);
+        kb = kb_ < nb ? kb_ : nb;
+        C = (nb + kb - 1) / kb;
+        kbl = nb - (C - 1) * kb;
+        cb = chunk_row_bytes(dt, kb);
+        cbl = chunk_row_bytes(dt, kbl);
+        ub = (int64_t)urows * ((C - 1) * cb + cbl);
+    }
+    __device__ void at(uint8_t *base, int64_t gr, int64_t b, uint8_t *&sc, uint8_t *&qu, uint8_t *&zpad, uint8_t *&zend) const {
+        const int QB = dtype == QMC_Q8_0 ? 32 : 16;
+        const int64_t u = gr / per, pos = gr % per + pos0, j = b / kb, bj = b % kb;
+        const int64_t kbj = j < C - 1 ? kb : kbl, cbj = j < C - 1 ? cb : cbl, sbj = (kbj * 2 + 15) / 16 * 16;
+        uint8_t *d = base + u * ub + (int64_t)urows * j * cb + pos * cbj;  // this row's chunk j
+        sc = d + 2 * bj;
+        qu = d + sbj + bj * QB;
+        zpad = zend = d + sbj;
+        if (bj == kbj - 1) zpad = d + 2 * kbj;
+    }
+};
+
+// one (row, block) per thread: the block's fp16 scale and quant bytes from the file layout (AoS) to
+// their places in the K-split layout
 __global__ void repack_chunked_kernel(int dtype, const uint8_t *__restrict__ aos, int64_t row0, int64_t rows, int64_t K,
                                       int kb, int urows, int per, int pos0, uint8_t *__restrict__ dst) {
-    const int64_t nb = nblocks(K);
+    const ChunkLayout L(dtype, K, kb, urows, per, pos0);
     const int BS = dtype == QMC_Q8_0 ? kQ8Bytes : kQ4Bytes, QB = BS - 2;
-    const int C = (int)((nb + kb - 1) / kb);
-    const int64_t kbl = nb - (int64_t)(C - 1) * kb, cb = chunk_row_bytes(dtype, kb), cbl = chunk_row_bytes(dtype, kbl);
-    const int64_t ub = (int64_t)urows * ((C - 1) * cb + cbl);  // bytes of a unit
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * nb; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / nb, b = i % nb, gr = row0 + r;
-        const int64_t u = gr / per, pos = gr % per + pos0;
-        const int j = (int)(b / kb), bj = (int)(b % kb);
-        const int64_t kbj = j < C - 1 ? kb : kbl, cbj = j < C - 1 ? cb : cbl, sbj = (kbj * 2 + 15) / 16 * 16;
-        uint8_t *d = dst + u * ub + (int64_t)urows * j * cb + pos * cbj;  // this row's chunk j
-        const uint8_t *s = aos + (r * nb + b) * BS;
-        d[2 * bj] = s[0];
-        d[2 * bj + 1] = s[1];
-        for (int k = 0; k < QB; k++) d[sbj + (int64_t)bj * QB + k] = s[2 + k];
-        if (bj == kbj - 1)
-            for (int64_t z = 2 * kbj; z < sbj; z++) d[z] = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * L.nb; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / L.nb, b = i % L.nb;
+        uint8_t *sc, *qu, *zp, *ze;
+        L.at(dst, row0 + r, b, sc, qu, zp, ze);
+        const uint8_t *s = aos + (r * L.nb + b) * BS;
+        sc[0] = s[0];
+        sc[1] = s[1];
+        for (int k = 0; k < QB; k++) qu[k] = s[2 + k];
+        for (uint8_t *z = zp; z < ze; z++) *z = 0;
+    }
+}
+
+// the same matrix from one K-split layout to another (e.g. chunks -> whole rows), block by block
+__global__ void relayout_chunked_kernel(int dtype, const uint8_t *__restrict__ src, int kb_src, uint8_t *__restrict__ dst,
+                                        int kb_dst, int64_t rows, int64_t K, int urows, int per, int pos0) {
+    const ChunkLayout Ls(dtype, K, kb_src, urows, per, pos0), Ld(dtype, K, kb_dst, urows, per, pos0);
+    const int QB = dtype == QMC_Q8_0 ? 32 : 16;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * Ld.nb; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / Ld.nb, b = i % Ld.nb;
+        uint8_t *ssc, *squ, *szp, *sze, *dsc, *dqu, *dzp, *dze;
+        Ls.at(const_cast<uint8_t *>(src), r, b, ssc, squ, szp, sze);
+        Ld.at(dst, r, b, dsc, dqu, dzp, dze);
+        dsc[0] = ssc[0];
+        dsc[1] = ssc[1];
+        for (int k = 0; k < QB; k++) dqu[k] = squ[k];
+        for (uint8_t *z = dzp; z < dze; z++) *z = 0;
     }
 }
 
@@ -1350,6 +1390,19 @@ int launch_repack_chunked(int dtype, const void *aos, int64_t row0, int64_t rows
     const int kbc = (int)std::min<int64_t>(kb, nblocks(K));
     repack_chunked_kernel<<<grid, 256, 0, s>>>(dtype, (const uint8_t *)aos, row0, rows, K, kbc, urows, per, pos0,
                                                (uint8_t *)dst);
+    QMC_LAUNCH_CHECK();
+    return QMC_OK;
+}
+
+int launch_relayout_chunked(int dtype, const void *src, int kb_src, void *dst, int kb_dst, int64_t rows, int64_t K,
+                            int urows, int per, int pos0, cudaStream_t s) {
+    if (dtype != QMC_Q8_0 && dtype != QMC_Q4_0) return set_error(QMC_EINVAL, "relayout: dtype %d is not quantized", dtype);
+    if (kb_src < 1 || kb_dst < 1 || urows < 1 || per < 1 || pos0 + per > urows) return set_error(QMC_EINVAL, "relayout: bad layout");
+    if (rows <= 0) return QMC_OK;
+    const int64_t work = rows * nblocks(K);
+    const int grid = (int)std::min<int64_t>((work + 255) / 256, 65536);
+    relayout_chunked_kernel<<<grid, 256, 0, s>>>(dtype, (const uint8_t *)src, kb_src, (uint8_t *)dst, kb_dst, rows, K, urows,
+                                                 per, pos0);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }

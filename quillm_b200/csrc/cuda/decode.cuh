@@ -100,6 +100,9 @@ __host__ __device__ inline int64_t chunk_row_bytes(int dtype, int64_t kb) {
 // own units)
 int launch_repack_chunked(int dtype, const void *aos, int64_t row0, int64_t rows, int64_t K, int kb, int urows, int per,
                           int pos0, void *dst, cudaStream_t s);
+// the same matrix (rows [0, rows), same unit mapping) from chunks of kb_src blocks to chunks of kb_dst
+int launch_relayout_chunked(int dtype, const void *src, int kb_src, void *dst, int kb_dst, int64_t rows, int64_t K,
+                            int urows, int per, int pos0, cudaStream_t s);
 // bytes of a unit of urows rows split into chunks of kb blocks
 __host__ __device__ inline int64_t chunked_unit_bytes(int dtype, int64_t K, int64_t kb, int urows) {
     const int64_t nb = (K + 31) / 32, k = kb < nb ? kb : nb, C = (nb + k - 1) / k;

@@ -40,6 +40,7 @@ struct Layer {
     // whole-row split copies for the tensor-core prefill: the same buffers as above, or, for a matrix
     // split along K, a second copy with whole rows
     uint8_t *pqkv = nullptr, *pwo = nullptr, *p13 = nullptr, *pw2 = nullptr;
+    bool pstale = true;  // the whole-row copies of K-split matrices predate the decode copies' last refill
     int dt[12];          // dtype per uploaded kind (indices QMC_T_*), -1 = missing
     unsigned dirty = 0;  // kinds (bit QMC_T_*) uploaded since the split-row copies were last refilled
     // blocks per K-chunk of the split copies (>= the row's blocks: whole rows), chosen with the ring plan
@@ -370,8 +371,9 @@ int setup_exchange(qmc_model *m) {
 // copies are released right after: the persistent path reads only the split-row copies (and the
 // tensor-core prefill the same), so the model holds its weights once.  A later upload of one tensor
 // allocates its file-layout buffer again, and only its rows are repacked.  A matrix split along K for
-// decode also keeps a whole-row copy for the tensor-core prefill (two copies), and the output matrix
-// keeps its file-layout copy (the batched prompt forward's final GEMV reads it).
+// decode gets a whole-row copy for the tensor-core prefill only when a batched prompt forward first
+// runs (prefill_copies), and the output matrix keeps its file-layout copy (the batched prompt forward's
+// final GEMV reads it).
 int repack_weights(qmc_model *m) {
     cudaStream_t s = m->stream;
     for (Layer &l : m->layers) {
@@ -382,41 +384,20 @@ int repack_weights(qmc_model *m) {
         if (!l.sqkv && (dalloc(m, (void **)&l.sqkv, (size_t)(nq / 2 * uq)) || dalloc(m, (void **)&l.swo, (size_t)(m->D * uo)) ||
                         dalloc(m, (void **)&l.s13, (size_t)(m->Hl * u13)) || dalloc(m, (void **)&l.sw2, (size_t)(m->D * u2))))
             return QMC_ENOMEM;
-        // the tensor-core prefill's whole-row copy of a K-split matrix (the same buffer otherwise)
-        const int64_t nbq = nblocks(m->D), nbo = nblocks(m->Dl), nbh = nblocks(m->Hl);
-        auto whole = [&](uint8_t **pc, uint8_t *sc, bool split, size_t bytes) -> int {
-            if (!split) {
-                *pc = sc;
-                return QMC_OK;
-            }
-            return *pc ? QMC_OK : dalloc(m, (void **)pc, bytes);
-        };
-        RC(whole(&l.pqkv, l.sqkv, l.kb_qkv < nbq, (size_t)(nq * split_row_bytes(dq, m->D))));
-        RC(whole(&l.pwo, l.swo, l.kb_wo < nbo, (size_t)(m->D * split_row_bytes(dw, m->Dl))));
-        RC(whole(&l.p13, l.s13, l.kb_13 < nbq, (size_t)(2 * m->Hl * split_row_bytes(d1, m->D))));
-        RC(whole(&l.pw2, l.sw2, l.kb_w2 < nbh, (size_t)(m->D * split_row_bytes(d2, m->Hl))));
+
         const unsigned d = l.dirty;
         if (!d) continue;
         // wq | wk | wv row ranges of the stacked matrix (pairs of consecutive rows are units)
         const int64_t q0[3] = {0, m->Dl, m->Dl + m->KVl}, qn[3] = {m->Dl, m->KVl, m->KVl};
         const int qk[3] = {QMC_T_WQ, QMC_T_WK, QMC_T_WV};
-        // each kind into the decode copy and, when that one is split along K, into the whole-row copy too
-        const int big = 1 << 30;
-        for (int pass = 0; pass < 2; pass++) {
-            const bool w = pass == 1;
-            for (int j = 0; j < 3; j++)
-                if ((d & (1u << qk[j])) && (!w || l.pqkv != l.sqkv))
-                    RC(launch_repack_chunked(dq, l.wqkv + q0[j] * aq, q0[j], qn[j], m->D, w ? big : l.kb_qkv, 2, 2, 0,
-                                             w ? l.pqkv : l.sqkv, s));
-            if ((d & (1u << QMC_T_WO)) && (!w || l.pwo != l.swo))
-                RC(launch_repack_chunked(dw, l.wo, 0, m->D, m->Dl, w ? big : l.kb_wo, 1, 1, 0, w ? l.pwo : l.swo, s));
-            if ((d & (1u << QMC_T_W1)) && (!w || l.p13 != l.s13))
-                RC(launch_repack_chunked(d1, l.w1, 0, m->Hl, m->D, w ? big : l.kb_13, 2, 1, 0, w ? l.p13 : l.s13, s));
-            if ((d & (1u << QMC_T_W3)) && (!w || l.p13 != l.s13))
-                RC(launch_repack_chunked(d1, l.w3, 0, m->Hl, m->D, w ? big : l.kb_13, 2, 1, 1, w ? l.p13 : l.s13, s));
-            if ((d & (1u << QMC_T_W2)) && (!w || l.pw2 != l.sw2))
-                RC(launch_repack_chunked(d2, l.w2, 0, m->D, m->Hl, w ? big : l.kb_w2, 1, 1, 0, w ? l.pw2 : l.sw2, s));
-        }
+        for (int j = 0; j < 3; j++)
+            if (d & (1u << qk[j]))
+                RC(launch_repack_chunked(dq, l.wqkv + q0[j] * aq, q0[j], qn[j], m->D, l.kb_qkv, 2, 2, 0, l.sqkv, s));
+        if (d & (1u << QMC_T_WO)) RC(launch_repack_chunked(dw, l.wo, 0, m->D, m->Dl, l.kb_wo, 1, 1, 0, l.swo, s));
+        if (d & (1u << QMC_T_W1)) RC(launch_repack_chunked(d1, l.w1, 0, m->Hl, m->D, l.kb_13, 2, 1, 0, l.s13, s));
+        if (d & (1u << QMC_T_W3)) RC(launch_repack_chunked(d1, l.w3, 0, m->Hl, m->D, l.kb_13, 2, 1, 1, l.s13, s));
+        if (d & (1u << QMC_T_W2)) RC(launch_repack_chunked(d2, l.w2, 0, m->D, m->Hl, l.kb_w2, 1, 1, 0, l.sw2, s));
+        l.pstale = true;
         QMC_CUDA(cudaStreamSynchronize(s));
         RC(dfree(m, &l.wqkv));
         RC(dfree(m, &l.wo));
@@ -431,6 +412,39 @@ int repack_weights(qmc_model *m) {
     m->out_dirty = false;
     QMC_CUDA(cudaStreamSynchronize(s));
     m->repacked = true;
+    return QMC_OK;
+}
+
+// The whole-row split copies the tensor-core prefill reads: a matrix decoded from whole rows shares its
+// decode copy; a K-split one gets a second copy, relaid out on the device from its chunks, allocated at
+// the first batched prompt forward and refreshed after any upload (a decode-only model never holds it).
+int prefill_copies(qmc_model *m) {
+    cudaStream_t s = m->stream;
+    const int big = 1 << 30;
+    for (Layer &l : m->layers) {
+        const int dq = l.dt[QMC_T_WQ], dw = l.dt[QMC_T_WO], d1 = l.dt[QMC_T_W1], d2 = l.dt[QMC_T_W2];
+        const int64_t nq = m->Dl + 2 * m->KVl;
+        const bool sq = l.kb_qkv < nblocks(m->D), so = l.kb_wo < nblocks(m->Dl), s1 = l.kb_13 < nblocks(m->D),
+                   s2 = l.kb_w2 < nblocks(m->Hl);
+        if (!sq) l.pqkv = l.sqkv;
+        if (!so) l.pwo = l.swo;
+        if (!s1) l.p13 = l.s13;
+        if (!s2) l.pw2 = l.sw2;
+        if (!l.pstale) continue;
+        if (sq && !l.pqkv) RC(dalloc(m, (void **)&l.pqkv, (size_t)(nq * split_row_bytes(dq, m->D))));
+        if (so && !l.pwo) RC(dalloc(m, (void **)&l.pwo, (size_t)(m->D * split_row_bytes(dw, m->Dl))));
+        if (s1 && !l.p13) RC(dalloc(m, (void **)&l.p13, (size_t)(2 * m->Hl * split_row_bytes(d1, m->D))));
+        if (s2 && !l.pw2) RC(dalloc(m, (void **)&l.pw2, (size_t)(m->D * split_row_bytes(d2, m->Hl))));
+        if (sq) RC(launch_relayout_chunked(dq, l.sqkv, l.kb_qkv, l.pqkv, big, nq, m->D, 2, 2, 0, s));
+        if (so) RC(launch_relayout_chunked(dw, l.swo, l.kb_wo, l.pwo, big, m->D, m->Dl, 1, 1, 0, s));
+        if (s1) {
+            RC(launch_relayout_chunked(d1, l.s13, l.kb_13, l.p13, big, m->Hl, m->D, 2, 1, 0, s));
+            RC(launch_relayout_chunked(d1, l.s13, l.kb_13, l.p13, big, m->Hl, m->D, 2, 1, 1, s));
+        }
+        if (s2) RC(launch_relayout_chunked(d2, l.sw2, l.kb_w2, l.pw2, big, m->D, m->Hl, 1, 1, 0, s));
+        l.pstale = false;
+    }
+    QMC_CUDA(cudaStreamSynchronize(s));
     return QMC_OK;
 }
 
@@ -955,6 +969,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     if (!complete(m)) return set_error(QMC_ESTATE, "prefill: model incomplete");
     RC(prepare_decode(m, c));  // quantized single-GPU models: the split-row copies the tensor cores read
     const bool tc = m->mega;  // the tensor-core contraction reads the whole-row split copies
+    if (tc) RC(prefill_copies(m));
     const int D = m->D, Dq = m->Dl, KVl = m->KVl, H = m->Hl, NQKV = Dq + 2 * KVl;
     const float eps = m->cfg.norm_eps;
     QMC_CUDA(cudaMemcpyAsync(m->pf_tok, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
