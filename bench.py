@@ -408,20 +408,20 @@ def gpu_arm(args, wl: dict) -> dict | None:
     e2e_sampled_s = d.max(time.perf_counter() - t0)
     sampler.close()
 
-    # batched prompt forward (single GPU): the same prompt through every layer at once, timed through
-    # the public call (host token copy in, logits copy out, one synchronisation)
-    prefill = None
-    if d.world == 1:
-        model.prefill(prompt, 0, logits)  # allocates the row buffers
-        reps = 5
-        e0.record(st)
-        for _ in range(reps):
-            model.prefill(prompt, 0, logits)
-        e1.record(st)
-        qb.check(qb.cuda().qmc_sync())
-        pf_s = e0.elapsed_time(e1) / 1e3 / reps
-        prefill = {"tokens": npos, "tok_s": npos / pf_s, "ms": pf_s * 1e3,
-                   "token_at_a_time_tok_s": npos / prompt_s, "speedup": prompt_s / pf_s}
+    # batched prompt forward: the same prompt through every layer at once, timed through the public call
+    # (host token copy in, logits copy out, one synchronisation); under tensor parallelism every rank
+    # runs it (its wo / w2 all-reduces are collectives) and the time is the max over ranks
+    model.prefill(prompt, 0, logits)  # allocates the row buffers
+    reps = 5
+    d.barrier()
+    e0.record(st)
+    for _ in range(reps):
+        model.prefill(prompt, 0, logits)
+    e1.record(st)
+    qb.check(qb.cuda().qmc_sync())
+    pf_s = d.max(e0.elapsed_time(e1) / 1e3 / reps)
+    prefill = {"tokens": npos, "tok_s": npos / pf_s, "ms": pf_s * 1e3,
+               "token_at_a_time_tok_s": npos / prompt_s, "speedup": prompt_s / pf_s}
 
     per_gpu_bytes = np.mean([model.step_bytes(p) for p in range(pos0, pos0 + K)])
     launches, persistent = model.decode_info()

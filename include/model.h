@@ -45,7 +45,8 @@ void qm_model_free(qm_model *m);
 float *qm_model_forward(qm_model *m, int32_t token, int32_t pos);
 /* batched prompt forward: tokens[0..n) at positions pos0 .. pos0+n-1 in one pass through every layer;
  * returns the model-owned logits of the last token (as qm_model_forward at pos0+n-1 after feeding the
- * prompt token by token, src/main.c:129) or NULL on bad arguments, a tensor-parallel model or a GPU error */
+ * prompt token by token, src/main.c:129) or NULL on bad arguments or a GPU error; under tensor
+ * parallelism every rank calls it with the same tokens */
 float *qm_model_prefill(qm_model *m, const int32_t *tokens, int32_t n, int32_t pos0);
 /* greedy generation kept on the device (prompt fed one token per step, then n_gen argmax tokens);
  * 0 on success */

@@ -157,9 +157,10 @@ int qmc_model_forward(qmc_model *m, int32_t token, int32_t pos, float *logits_ho
 /* batched prompt forward: tokens[0..n) at positions pos0 .. pos0+n-1 through every layer together (each
  * matrix applied once to all n rows), filling those KV-cache slots; logits_host / next_token receive the
  * last token's logits and greedy argmax, as qmc_model_forward at pos0+n-1 would after feeding the prompt
- * one token at a time.  Replaces the reference's token-at-a-time prompt loop (src/main.c:129); single-GPU
- * models only (QMC_EINVAL under tensor parallelism).  Row buffers for n tokens are allocated on the first
- * call that needs them. */
+ * one token at a time.  Replaces the reference's token-at-a-time prompt loop (src/main.c:129).  Under
+ * tensor parallelism every rank calls it with the same tokens (collective: the wo / w2 partial sums are
+ * all-reduced, the logits all-gathered).  Row buffers for n tokens are allocated on the first call that
+ * needs them. */
 int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t pos0, float *logits_host,
                       int32_t *next_token);
 /* greedy generation kept on the device: feeds prompt[0..n_prompt) one token per step from position 0,

@@ -947,6 +947,13 @@ int prefill_proj_tc(qmc_model *m, int dt, const uint8_t *Ws, const float *A, int
     if (A) RC(launch_quantize_act(A, T, K, m->pf_aq, m->pf_ad, m->stream, m->pf_adT, matmul_tc_scale_ld(T)));
     return launch_matmul_q_tc(dt, Ws, split_row_bytes(dt, K), m->pf_aq, m->pf_adT, C, C2, T, N, K, ctx()->err, m->stream);
 }
+// tensor parallelism: the wo / w2 contraction of a rank covers its column shard (its heads, its hidden
+// rows), so pf_c holds a partial sum of every row; the ranks' partials are summed in place (NCCL) before
+// the residual add, as the decode step adds them after its wo / w2 epilogues
+int prefill_all_reduce(qmc_model *m, int T, const char *what) {
+    if (m->tp == 1) return QMC_OK;
+    return nccl_check(ncclAllReduce(m->pf_c, m->pf_c, (size_t)T * m->D, ncclFloat, ncclSum, m->comm, m->stream), what);
+}
 // x += add (when given), then rmsnorm(x) * w straight into the activation blocks of the next tensor-core
 // contraction
 int prefill_norm_quant(qmc_model *m, const float *add, const float *w, int T) {
@@ -959,7 +966,6 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
                       int32_t *next_token) {
     if (!m || !tokens || n < 1 || pos0 < 0 || (int64_t)pos0 + n > m->S)
         return set_error(QMC_EINVAL, "prefill: bad arguments (n %d, pos0 %d, max_seq %d)", n, pos0, m ? m->S : 0);
-    if (m->tp != 1) return set_error(QMC_EINVAL, "prefill: tensor-parallel models decode the prompt token by token");
     for (int i = 0; i < n; i++)
         if (tokens[i] < 0 || tokens[i] >= m->V) return set_error(QMC_EINVAL, "prefill: token %d out of range", tokens[i]);
     RC(check_dev(m));
@@ -967,7 +973,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     cudaStream_t s = m->stream;
     DevCtx *c = ctx();
     if (!complete(m)) return set_error(QMC_ESTATE, "prefill: model incomplete");
-    RC(prepare_decode(m, c));  // quantized single-GPU models: the split-row copies the tensor cores read
+    RC(prepare_decode(m, c));  // quantized models on the single-launch path: the split-row copies the tensor cores read
     const bool tc = m->mega;  // the tensor-core contraction reads the whole-row split copies
     if (tc) RC(prefill_copies(m));
     const int D = m->D, Dq = m->Dl, KVl = m->KVl, H = m->Hl, NQKV = Dq + 2 * KVl;
@@ -989,6 +995,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
                                vcl, m->kv16 != 0, m->pf_att, s));
         if (tc) RC(prefill_proj_tc(m, Ly.dt[QMC_T_WO], Ly.pwo, m->pf_att, n, D, Dq, m->pf_c, nullptr));
         else RC(prefill_proj(m, Ly.dt[QMC_T_WO], Ly.wo, m->pf_att, n, D, Dq, m->pf_c));
+        RC(prefill_all_reduce(m, n, "all-reduce(prefill wo)"));
         if (tc) {  // wo residual fused with the norm
             RC(prefill_norm_quant(m, m->pf_c, Ly.ffn_norm, n));
             RC(prefill_proj_tc(m, Ly.dt[QMC_T_W1], Ly.p13, nullptr, n, 2 * (int64_t)H, D, m->pf_h, m->pf_h3));
@@ -1005,6 +1012,7 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
             RC(launch_swiglu(m->pf_h, m->pf_h3, (int64_t)n * H, s));
             RC(prefill_proj(m, Ly.dt[QMC_T_W2], Ly.w2, m->pf_h, n, D, H, m->pf_c));
         }
+        RC(prefill_all_reduce(m, n, "all-reduce(prefill w2)"));
         // w2 residual: on the tensor-core path the next layer's norm adds it, except after the last layer
         if (!tc || l == m->L - 1) RC(launch_add(m->pf_x, m->pf_c, (int64_t)n * D, s));
     }
@@ -1017,10 +1025,12 @@ int qmc_model_prefill(qmc_model *m, const int32_t *tokens, int32_t n, int32_t po
     g.x = m->pf_x + (int64_t)(n - 1) * D;
     g.norm_w = m->norm;
     g.eps = eps;
-    g.y = m->logits;
+    g.y = m->logits_l;
     g.epi = EPI_STORE;
     g.err = c->err;
     RC(launch_gemv(g, s, false));
+    if (m->tp > 1)
+        RC(nccl_check(ncclAllGather(m->logits_l, m->logits, m->Vl, ncclFloat, m->comm, s), "all-gather(prefill logits)"));
     QMC_CUDA(cudaMemcpyAsync(m->h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s));
     QMC_CUDA(cudaStreamSynchronize(s));
     RC(qmc_check_device_error());

@@ -54,7 +54,8 @@ def test_two_gloo_ranks_share_id_and_reduce_max(tmp_path):
 def test_tp_matches_single_gpu(tmp_path, world):
     """tensor-parallel decode over 2, 4 or 8 GPUs (NCCL, one process per GPU; GQA group 2, so at 8 ranks
     each holds one KV head and its two query heads) gives the single-GPU tokens and logits within the
-    reference's tolerance (tests/test_model.c:50-53, 2e-2 relative)"""
+    reference's tolerance (tests/test_model.c:50-53, 2e-2 relative); so does the tensor-parallel batched
+    prompt forward (qm_model_prefill), and the greedy decode that continues from it"""
     import torch
 
     if torch.cuda.device_count() < world:
@@ -87,13 +88,21 @@ for tp in ((1, 0), (world, rank)):
     for p in range(12):
         t = m.forward(t, p, lg)
         toks.append(t)
-    outs.append((toks, lg.copy()))
+    # the batched prompt forward over the same cache slots, then greedy decode from its token
+    lp = np.zeros(cfg["vocab_size"], np.float32)
+    t = m.prefill([(7 * i + 3) % cfg["vocab_size"] for i in range(20)], 0, lp)
+    ptoks = [t]
+    for p in range(20, 24):
+        t = m.forward(t, p)
+        ptoks.append(t)
+    outs.append((toks, lg.copy(), ptoks, lp))
     m.close()
 dist.barrier()
 if rank == 0:
-    (t1, l1), (t2, l2) = outs
+    (t1, l1, p1, lp1), (t2, l2, p2, lp2) = outs
     rel = float(np.max(np.abs(l1 - l2)) / np.max(np.abs(l1)))
-    open({str(tmp_path / "res.txt")!r}, "w").write(f"{{t1 == t2}} {{rel}}")
+    prel = float(np.max(np.abs(lp1 - lp2)) / np.max(np.abs(lp1)))
+    open({str(tmp_path / "res.txt")!r}, "w").write(f"{{t1 == t2}} {{rel}} {{p1 == p2}} {{prel}}")
 dist.destroy_process_group()
 """)
     port = _free_port()
@@ -101,7 +110,8 @@ dist.destroy_process_group()
            "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(port), str(script)]
     r = subprocess.run(cmd, capture_output=True, text=True, env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     assert r.returncode == 0, r.stderr[-3000:]
-    same, rel = open(tmp_path / "res.txt").read().split()
-    print(f"tp{world} vs tp1: identical greedy tokens {same}, max rel logit diff {float(rel):.2e}")
-    assert same == "True"
-    assert float(rel) < 2e-2
+    same, rel, psame, prel = open(tmp_path / "res.txt").read().split()
+    print(f"tp{world} vs tp1: identical greedy tokens {same}, max rel logit diff {float(rel):.2e}; "
+          f"batched prompt forward: identical tokens after it {psame}, last-token rel logit diff {float(prel):.2e}")
+    assert same == "True" and psame == "True"
+    assert float(rel) < 2e-2 and float(prel) < 2e-2
