@@ -25,6 +25,7 @@
 
 #include <algorithm>
 
+#include "actquant.cuh"
 #include "gemv.cuh"
 
 namespace qmc {
@@ -33,7 +34,6 @@ namespace {
 constexpr int NCW = 16;              // consumer warps
 constexpr int NG = 4, GW = 4;        // consumer groups x warps per group (NG * GW == NCW)
 constexpr int NT = (NCW + 1) * 32;   // + one producer warp
-constexpr int CH = 4096;             // activation staging chunk (floats)
 constexpr int kStageTarget = 16 * 1024;
 constexpr int kCoResidentSmem = 112 * 1024;  // two CTAs (this kernel and the next) per SM
 // Matrices of at least this many bytes take the whole shared memory of the SM for their ring (up to
@@ -50,7 +50,7 @@ struct KParams {
     int urows;        // rows per unit (2 for QKV pairs and for SwiGLU's w1/w3 rows)
     int R, g;         // units per stage; warps per unit (g = 4 / R when R < 4, else 1)
     int stage_bytes, part_bytes, nstages;  // part_bytes: offset of the w3 copy inside a SwiGLU stage
-    int off_bars, off_xq, off_xds, off_xs, off_red;  // shared-memory offsets
+    int off_bars, off_xq, off_xds, off_red;  // shared-memory offsets
     const float *x, *norm_w;
     float eps;
     int epi;
@@ -87,7 +87,8 @@ __device__ __forceinline__ CopyPlan plan_copy(int64_t start, int64_t len, int64_
 
 // stage k of a CTA whose units start at u0: units [u0 + kR, u0 + kR + R) as one contiguous copy (two for
 // SwiGLU's separate w1/w3 matrices), 16-byte lines by bulk copy plus tail bytes by plain stores
-__device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int64_t u0, int64_t u1, int k) {
+__device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int64_t u0, int64_t u1, int k,
+                            uint64_t pol) {
     const int64_t ua = u0 + (int64_t)k * p.R;
     const int64_t n = min((int64_t)p.R, u1 - ua);
     const uint8_t *src[2];
@@ -115,7 +116,7 @@ __device__ void issue_stage(const KParams &p, uint8_t *stage, uint64_t *bar, int
     if (plain) fence_proxy_async();
     mbar_arrive_tx(bar, tx);
     for (int i = 0; i < parts; i++)
-        if (cp[i].tma) bulk_g2s(dst[i], src[i] + cp[i].a0, cp[i].tma, bar);
+        if (cp[i].tma) bulk_g2s_hint(dst[i], src[i] + cp[i].a0, cp[i].tma, bar, pol);
 }
 
 __device__ __forceinline__ void named_sync(int id, int threads) {
@@ -132,9 +133,7 @@ __device__ __forceinline__ void load_words(const uint8_t *bp, uint32_t (&w)[NW],
     for (int i = 0; i < NW; i++) w[i] = wp[i];
 }
 
-// 32 activation bytes of block b as 8 words.  The prologue stores the two 16-byte halves of block b
-// swapped when bit 2 of b is set, so the 8 lanes of a quarter-warp (consecutive b) hit all 32 banks.
-__device__ __forceinline__ int xswz(int b) { return ((b >> 2) & 1) << 4; }
+// 32 activation bytes of block b as 8 words (stored with the xswz bank swizzle of actquant.cuh)
 __device__ __forceinline__ void load_x(const uint8_t *xq, int b, uint32_t (&xw)[8]) {
     const uint8_t *p = xq + (int64_t)b * 32;
     const int sw = xswz(b);
@@ -204,83 +203,76 @@ __device__ __forceinline__ void epilogue(const KParams &p, int64_t unit, float a
 }
 
 // ---------------------------------------------------------------- prologue: rmsnorm + quantize
-// x is staged through shared memory in CH-float chunks with wide independent loads; with norm_w the
-// values become x * inv * w, inv = (float)(1 / sqrt(sum_double(x^2)/n + eps)) (src/ops.c:93-98).
-// Quantized activations go to shared memory: int8 (Q4_0: even elements then odd elements per block),
-// and (fp32 scale, int block sum) pairs.
-__device__ __forceinline__ void stage_chunk(float *xs, const float *src, int c0, int n) {
-    const int t = threadIdx.x;
-    if (((uintptr_t)(src + c0) & 15) == 0) {
-        const int n4 = n >> 2;
-        const float4 *s4 = (const float4 *)(src + c0);
-        for (int i = t; i < n4; i += NT) ((float4 *)xs)[i] = s4[i];
-        for (int i = (n4 << 2) + t; i < n; i += NT) xs[i] = src[c0 + i];
+// The consumer warps quantize the activations, four threads per block (8 elements each; quant_block<8>),
+// NCW * 8 blocks a round: the values
+// come straight from global memory into registers, and the next round's loads are issued before the
+// current round is quantized.  With norm_w the values become x * inv * w, inv = (float)(1 / sqrt(
+// sum_double(x^2)/n + eps)) (src/ops.c:93-98); a row of one round keeps x in registers across the block
+// sum, longer rows take a first pass for the sum.  Quantized activations go to shared memory (int8
+// blocks, Q4_0 with even elements then odd ones, and (fp32 scale, int block sum) pairs); CTA 0 also
+// writes the Q8_0 blocks to xq_out.  x and norm_w are caller pointers: vector loads only where the 8
+// elements are in range and 16-byte aligned.
+constexpr int QE = 8;              // elements per thread
+constexpr int NCT = NCW * 32;      // consumer threads (the prologue's)
+constexpr int QB = NCT / 4;        // blocks per round
+constexpr int kBarPrologue = 14;   // named barrier of the consumer threads (1..8: unit groups, 15: argmax)
+__device__ __forceinline__ void load8(const float *x, int64_t e0, int K, float (&v)[QE]) {
+    if (e0 + QE <= K && ((uintptr_t)(x + e0) & 15) == 0) {
+        const float4 a = ((const float4 *)(x + e0))[0], c = ((const float4 *)(x + e0))[1];
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
     } else {
-        for (int i = t; i < n; i += NT) xs[i] = src[c0 + i];
+#pragma unroll
+        for (int i = 0; i < QE; i++) v[i] = e0 + i < K ? x[e0 + i] : 0.0f;
     }
 }
 
 template <int DT>
 __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    float *xs = (float *)(sm + p.off_xs);
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, qd = t >> 2, j = t & 3;
     float *red = (float *)(sm + p.off_red);
     uint8_t *xq = sm + p.off_xq;
     int2 *xds = (int2 *)(sm + p.off_xds);
-    const int nchunk = (p.K + CH - 1) / CH;
+    uint8_t *aos = p.xq_out && blockIdx.x == 0 ? p.xq_out : nullptr;  // every CTA holds the same blocks
+    const int rounds = (p.nb + QB - 1) / QB;
+    auto at = [&](int r) { return (int64_t)(r * QB + qd) * 32 + QE * j; };
+    float v[QE], nx[QE];
     float inv = 1.0f;
     if (p.norm_w) {
         double ss = 0.0;
-        for (int c = 0; c < nchunk; c++) {
-            const int c0 = c * CH, n = min(CH, p.K - c0);
-            if (nchunk > 1) __syncthreads();
-            stage_chunk(xs, p.x, c0, n);
-            __syncthreads();
-            for (int i = t; i < n; i += NT) ss += (double)xs[i] * (double)xs[i];
+        for (int r = 0; r < rounds; r++) {
+            load8(p.x, at(r), p.K, v);
+#pragma unroll
+            for (int i = 0; i < QE; i++) ss += (double)v[i] * (double)v[i];
         }
         ss = warp_sum_d(ss);
         double *dred = (double *)red;
-        __syncthreads();
         if (lane == 0) dred[warp] = ss;
-        __syncthreads();
+        named_sync(kBarPrologue, NCT);
         if (t == 0) {
-            double s = 0.0;
-            for (int w = 0; w < NT / 32; w++) s += dred[w];
-            red[2 * NT / 32] = (float)(1.0 / sqrt(s / (double)p.K + (double)p.eps));
+            double tot = 0.0;
+            for (int w = 0; w < NCW; w++) tot += dred[w];
+            red[2 * NT / 32] = (float)(1.0 / sqrt(tot / (double)p.K + (double)p.eps));
         }
-        __syncthreads();
+        named_sync(kBarPrologue, NCT);
         inv = red[2 * NT / 32];
+        if (rounds > 1) load8(p.x, at(0), p.K, v);  // one round: x is still in v
+    } else {
+        load8(p.x, at(0), p.K, v);
     }
-    for (int c = 0; c < nchunk; c++) {
-        const int c0 = c * CH, n = min(CH, p.K - c0);
-        if (!(p.norm_w && nchunk == 1)) {  // single-chunk norm: x is still staged
-            __syncthreads();
-            stage_chunk(xs, p.x, c0, n);
+    for (int r = 0; r < rounds; r++) {
+        if (r + 1 < rounds) load8(p.x, at(r + 1), p.K, nx);
+        if (p.norm_w) {
+            float w[QE];
+            load8(p.norm_w, at(r), p.K, w);
+#pragma unroll
+            for (int i = 0; i < QE; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
         }
-        __syncthreads();
-        const int b0 = c0 / 32, nbc = (n + 31) / 32;
-        for (int bb = warp; bb < nbc; bb += NT / 32) {
-            const int b = b0 + bb, i = bb * 32 + lane;
-            float v = 0.0f;
-            if (i < n) {
-                v = xs[i];
-                if (p.norm_w) v = __fmul_rn(__fmul_rn(v, inv), p.norm_w[c0 + i]);
-            }
-            float dd;
-            uint32_t dh;
-            const int qv = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
-            const int pos_in_block = DT == QMC_Q4_0 ? ((lane & 1) ? 16 : 0) + (lane >> 3) * 4 + ((lane & 7) >> 1) : lane;
-            xq[b * 32 + (pos_in_block ^ xswz(b))] = (uint8_t)(int8_t)qv;
-            const int bs = __reduce_add_sync(0xffffffffu, qv);
-            if (lane == 0) xds[b] = make_int2(__float_as_int(dd), bs);
-            if (p.xq_out && blockIdx.x == 0) {  // every CTA holds the same blocks; one writes them
-                uint8_t *blk = p.xq_out + (int64_t)b * kQ8Bytes;
-                blk[2 + lane] = (uint8_t)(int8_t)qv;
-                if (lane == 0) blk[0] = (uint8_t)(dh & 0xff), blk[1] = (uint8_t)(dh >> 8);
-            }
-        }
+        const int b = r * QB + qd;
+        quant_block<QE>(DT == QMC_Q4_0, xq, xds, b, j, b < p.nb, v, aos);
+#pragma unroll
+        for (int i = 0; i < QE; i++) v[i] = nx[i];
     }
-    __syncthreads();
+    named_sync(kBarPrologue, NCT);
 }
 
 // EPI_LOGITS tail (consumer warps only): CTA max of the warps' keys, one atomicMax per CTA, and the
@@ -323,22 +315,24 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
         fence_mbar_init();
     }
     __syncthreads();
-    if (warp == NCW && lane == 0)  // weights do not depend on the previous kernel: prefetch first
-        for (int k = 0; k < p.nstages && k < nst; k++) issue_stage(p, sm + (int64_t)k * p.stage_bytes, &full[k], u0, u1, k);
-    pdl_wait();
-    prologue_quant<DT>(p, sm);
-    pdl_launch_dependents();
-
-    if (warp == NCW) {  // producer: refill each stage once its consumers released it
+    // each weight byte is read once: its lines are the first L2 evicts, so the activations (the previous
+    // kernel's output) and the other operands stay in L2 across a chain of matvecs
+    const uint64_t pol = l2_evict_first_policy();
+    // The producer warp takes no part in the activation prologue: its first copies may wait for room in
+    // the copy queue, and a prologue barrier that included it would hold every consumer warp behind them.
+    // Weights do not depend on the previous kernel, so the ring fills before (and while) it finishes.
+    if (warp == NCW) {
         if (lane == 0) {
-            int k = min(p.nstages, nst);  // stages issued so far
+            for (int k = 0; k < p.nstages && k < nst; k++)
+                issue_stage(p, sm + (int64_t)k * p.stage_bytes, &full[k], u0, u1, k, pol);
+            int k = min(p.nstages, nst);  // stages issued so far; refill each once its consumers release it
             for (; k < nst; k++) {
                 const int s = k % p.nstages;
                 if (!mbar_wait(&empty[s], (uint32_t)((k / p.nstages) - 1) & 1u)) {
                     raise_error(p.err, kErrMbarTimeout);
                     break;
                 }
-                issue_stage(p, sm + (int64_t)s * p.stage_bytes, &full[s], u0, u1, k);
+                issue_stage(p, sm + (int64_t)s * p.stage_bytes, &full[s], u0, u1, k, pol);
             }
             // drain: the last copy of each slot may still be in flight; consumers that timed out will not
             // wait for it, and the CTA must not exit before it lands (bounded)
@@ -351,6 +345,10 @@ __global__ void __launch_bounds__(NT, 2) gemv_q_kernel(const KParams p) {
         }
         return;
     }
+
+    pdl_wait();
+    prologue_quant<DT>(p, sm);
+    pdl_launch_dependents();
 
     constexpr int BS = DT == QMC_Q8_0 ? kQ8Bytes : kQ4Bytes;
     const uint8_t *xq = sm + p.off_xq;
@@ -546,7 +544,7 @@ int launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl, int grid_limit
         p.stage_bytes = (int)(((int64_t)p.R * unit_bytes + 48 + 127) & ~(int64_t)127);
     }
     const int xq_bytes = ((p.nb * 32 + 127) / 128) * 128, xds_bytes = ((p.nb * 8 + 127) / 128) * 128;
-    const int fixed = xq_bytes + xds_bytes + CH * 4 + 2 * NT * 4 + 256;  // red: 2 x 16 float2 + 16 keys
+    const int fixed = xq_bytes + xds_bytes + 2 * NT * 4 + 256;  // red: 2 x 16 float2 + 16 keys
     // prefer a footprint that lets the next kernel's CTA co-reside (its weight prefetch then overlaps this
     // kernel's tail); very long rows fall back to the whole shared memory of the SM
     // nstages is a multiple of NG so every slot belongs to one group (slot s serves stages s, s + ns, ...,
@@ -562,8 +560,7 @@ int launch_gemv(const GemvArgs &a, cudaStream_t stream, bool pdl, int grid_limit
     p.off_bars = ns * p.stage_bytes;
     p.off_xq = p.off_bars + ((2 * ns * 8 + 127) / 128) * 128;
     p.off_xds = p.off_xq + xq_bytes;
-    p.off_xs = p.off_xds + xds_bytes;
-    p.off_red = p.off_xs + CH * 4;
+    p.off_red = p.off_xds + xds_bytes;
     const size_t smem = (size_t)p.off_red + 2 * NT * 4 + 256;
     const int which = a.dtype == QMC_Q8_0 ? 0 : 1;
     if (!g_attr_done[c->device][which]) {
