@@ -34,15 +34,13 @@ __device__ __forceinline__ int quant_near_half(float v, float r, float sc) {
     return min(127, max(-127, q));
 }
 
-// Q8_0 of block b held by 32 / E lanes (part j: elements E j .. E j + E - 1; E = 16, a lane pair, or 8,
-// a lane quad), bit-exact with src/quant.c:33-53: amax ignores NaN, IEEE division for the scale, fp16
-// RNE scale, then rint(v / scale) clamped to +-127 (NaN -> 0, as the float->int conversion gives).  All
-// lanes call it (shuffles within the lane group); `active` lanes store.  Q4_0 weights take the block's
-// even elements in bytes 0-15 and odd elements in bytes 16-31.  With `aos`, the active lanes also
-// write the block in the .qlm Q8_0 layout at aos + 34 b.
-template <int E = 16>
-__device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int b, int j, bool active,
-                                            const float (&v)[E], uint8_t *aos = nullptr) {
+// The arithmetic of one Q8_0 block held by 32 / E lanes (part j: elements E j .. E j + E - 1; E = 16, a
+// lane pair, or 8, a lane quad), bit-exact with src/quant.c:33-53: amax ignores NaN, IEEE division for
+// the scale, fp16 RNE scale, then rint(v / scale) clamped to +-127 (NaN -> 0, as the float->int
+// conversion gives).  All lanes call it (shuffles within the lane group).  Out: the lane's quants in
+// element order (4 per word), the block's quant sum (every lane of the group) and its scale.
+template <int E>
+__device__ __forceinline__ void quant_group(const float (&v)[E], uint32_t (&w)[E / 4], int &sum, float &sc) {
     static_assert(E == 16 || E == 8, "a block is held by 2 or 4 lanes");
     constexpr int NWD = E / 4;  // quant words per lane
     uint32_t m[E / 2];
@@ -58,16 +56,15 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
     uint32_t ab = m[0];
 #pragma unroll
     for (int o = 1; o < 32 / E; o <<= 1) ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, o));
-    const float sc = h2f(f2h(__fdiv_rn(__uint_as_float(ab), 127.0f)));
+    sc = h2f(f2h(__fdiv_rn(__uint_as_float(ab), 127.0f)));
     const float rs = __frcp_rn(sc);
     // q = rint(v / sc) clamped to +-127, as v * (1 / sc) + 1.5 * 2^23 (round to nearest even, no
     // float->int conversion).  |v / sc| < 256, so v * (1 / sc) lies within 4.6e-5 of the correctly
     // rounded quotient and rounds to the same integer unless it is within 1e-4 of a half-integer; those
     // elements take quant_near_half.  NaN gives 0.
-    uint32_t w[NWD];  // the lane's quants in element order, 4 per word
 #pragma unroll
-    for (int i = 0; i < NWD; i++) w[i] = 0u;
-    int sum = 0;
+    for (int i = 0; i < NWD; i++) w[i] = 0u;  // the lane's quants in element order, 4 per word
+    sum = 0;
     bool near = false;
 #pragma unroll
     for (int i = 0; i < E; i++) {
@@ -95,6 +92,20 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
     }
 #pragma unroll
     for (int o = 1; o < 32 / E; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+}
+
+// Block b (quant_group) stored where the dot loops read it: int8 at xq + 32 b with the xswz swizzle, the
+// (scale, quant sum) pair at xds[b].  All lanes call it; `active` lanes store.  Q4_0 weights take the
+// block's even elements in bytes 0-15 and odd elements in bytes 16-31.  With `aos`, the active lanes
+// also write the block in the .qlm Q8_0 layout at aos + 34 b.
+template <int E = 16>
+__device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int b, int j, bool active,
+                                            const float (&v)[E], uint8_t *aos = nullptr) {
+    constexpr int NWD = E / 4;  // quant words per lane
+    uint32_t w[NWD];
+    int sum;
+    float sc;
+    quant_group<E>(v, w, sum, sc);
     if (!active) return;
     uint8_t *blk = xq + (int64_t)b * 32;
     const int sw = xswz(b);
@@ -124,6 +135,52 @@ __device__ __forceinline__ void quant_block(bool q4, uint8_t *xq, int2 *xds, int
         }
 #pragma unroll
         for (int i = 0; i < E; i++) o[2 + E * j + i] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+    }
+}
+
+// 8 floats x[e0 .. e0 + 8), zero past n: two vector loads where the 8 are in range and 16-byte aligned
+__device__ __forceinline__ void load8_any(const float *x, int64_t e0, int64_t n, float (&v)[8]) {
+    if (e0 + 8 <= n && ((uintptr_t)(x + e0) & 15) == 0) {
+        const float4 a = ((const float4 *)(x + e0))[0], c = ((const float4 *)(x + e0))[1];
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = e0 + i < n ? x[e0 + i] : 0.0f;
+    }
+}
+
+// Q8_0 of T rows of n floats by lane quads (quant_group<8>) into the row-major activation blocks of the
+// prefill contractions: qs[t][nb][32] int8 in element order, d[t][nb] scales and, with dT, the scales
+// again block-major at dT[b * ldT + t].  fetch(t, e0, v) gives elements e0 .. e0 + 7 of row t (zero past
+// n).  A warp takes 8 consecutive blocks per step, so its lanes stay together for the quad shuffles.
+template <class Fetch>
+__device__ __forceinline__ void quant_rows_quads(int64_t T, int64_t n, Fetch &&fetch, int8_t *qs, float *d, float *dT,
+                                                 int64_t ldT) {
+    const int lane = threadIdx.x & 31, j = lane & 3;
+    const int64_t nb = nblocks(n), total = T * nb;
+    const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t base = w0 * 8; base < total; base += nw * 8) {
+        const int64_t blk = base + (lane >> 2);
+        const bool active = blk < total;
+        const int64_t t = active ? blk / nb : 0, b = active ? blk % nb : 0;
+        float v[8];
+        if (active) {
+            fetch(t, b * 32 + 8 * j, v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = 0.0f;
+        }
+        uint32_t w[2];
+        int sum;
+        float sc;
+        quant_group<8>(v, w, sum, sc);
+        if (active) {
+            *(uint2 *)(qs + (t * nb + b) * 32 + 8 * j) = make_uint2(w[0], w[1]);
+            if (j == 0) {
+                d[t * nb + b] = sc;
+                if (dT) dT[b * ldT + t] = sc;
+            }
+        }
     }
 }
 

@@ -211,21 +211,11 @@ __device__ __forceinline__ void epilogue(const KParams &p, int64_t unit, float a
 // sum, longer rows take a first pass for the sum.  Quantized activations go to shared memory (int8
 // blocks, Q4_0 with even elements then odd ones, and (fp32 scale, int block sum) pairs); CTA 0 also
 // writes the Q8_0 blocks to xq_out.  x and norm_w are caller pointers: vector loads only where the 8
-// elements are in range and 16-byte aligned.
+// elements are in range and 16-byte aligned (load8_any).
 constexpr int QE = 8;              // elements per thread
 constexpr int NCT = NCW * 32;      // consumer threads (the prologue's)
 constexpr int QB = NCT / 4;        // blocks per round
 constexpr int kBarPrologue = 14;   // named barrier of the consumer threads (1..8: unit groups, 15: argmax)
-__device__ __forceinline__ void load8(const float *x, int64_t e0, int K, float (&v)[QE]) {
-    if (e0 + QE <= K && ((uintptr_t)(x + e0) & 15) == 0) {
-        const float4 a = ((const float4 *)(x + e0))[0], c = ((const float4 *)(x + e0))[1];
-        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
-    } else {
-#pragma unroll
-        for (int i = 0; i < QE; i++) v[i] = e0 + i < K ? x[e0 + i] : 0.0f;
-    }
-}
-
 template <int DT>
 __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5, qd = t >> 2, j = t & 3;
@@ -240,7 +230,7 @@ __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
     if (p.norm_w) {
         double ss = 0.0;
         for (int r = 0; r < rounds; r++) {
-            load8(p.x, at(r), p.K, v);
+            load8_any(p.x, at(r), p.K, v);
 #pragma unroll
             for (int i = 0; i < QE; i++) ss += (double)v[i] * (double)v[i];
         }
@@ -255,15 +245,15 @@ __device__ void prologue_quant(const KParams &p, uint8_t *sm) {
         }
         named_sync(kBarPrologue, NCT);
         inv = red[2 * NT / 32];
-        if (rounds > 1) load8(p.x, at(0), p.K, v);  // one round: x is still in v
+        if (rounds > 1) load8_any(p.x, at(0), p.K, v);  // one round: x is still in v
     } else {
-        load8(p.x, at(0), p.K, v);
+        load8_any(p.x, at(0), p.K, v);
     }
     for (int r = 0; r < rounds; r++) {
-        if (r + 1 < rounds) load8(p.x, at(r + 1), p.K, nx);
+        if (r + 1 < rounds) load8_any(p.x, at(r + 1), p.K, nx);
         if (p.norm_w) {
             float w[QE];
-            load8(p.norm_w, at(r), p.K, w);
+            load8_any(p.norm_w, at(r), p.K, w);
 #pragma unroll
             for (int i = 0; i < QE; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), w[i]);
         }

@@ -9,6 +9,7 @@
 // scalar matvec bit for bit.
 //
 // gemm_f32: the f32 contract of qm_matmul_nt (src/ops.c:81-91), 64x64 tiles, 4x4 per thread.
+#include "actquant.cuh"
 #include "matmul.cuh"
 
 namespace qmc {
@@ -20,21 +21,8 @@ constexpr int WS = KB * 8 + 1;  // padded row stride in 32-bit words
 
 __global__ void quantize_act_kernel(const float *__restrict__ x, int64_t T, int64_t K, int8_t *__restrict__ qs,
                                     float *__restrict__ d, float *__restrict__ dT, int64_t ldT) {
-    const int lane = threadIdx.x & 31;
-    const int64_t nb = nblocks(K);
-    const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t blk = w0; blk < T * nb; blk += nw) {
-        const int64_t t = blk / nb, b = blk % nb, c = b * 32 + lane;
-        const float v = c < K ? x[t * K + c] : 0.0f;
-        float dd;
-        uint32_t dh;
-        const int q = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
-        qs[t * nb * 32 + c] = (int8_t)q;
-        if (lane == 0) {
-            d[t * nb + b] = dd;
-            if (dT) dT[b * ldT + t] = dd;
-        }
-    }
+    quant_rows_quads(
+        T, K, [&](int64_t t, int64_t e0, float (&v)[8]) { load8_any(x + t * K, e0, K, v); }, qs, d, dT, ldT);
 }
 
 template <int DT>
@@ -173,8 +161,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float *__restrict__
 
 int launch_quantize_act(const float *x, int64_t T, int64_t K, int8_t *qs, float *d, cudaStream_t s, float *dT,
                         int64_t ldT) {
-    const int64_t warps = T * nblocks(K);
-    const int64_t grid = (warps * 32 + 255) / 256;
+    const int64_t grid = (T * nblocks(K) * 4 + 255) / 256;  // a thread per 8 elements (the loop covers the rest)
     quantize_act_kernel<<<(int)(grid < 65535 ? grid : 65535), 256, 0, s>>>(x, T, K, qs, d, dT, ldT);
     QMC_LAUNCH_CHECK();
     return QMC_OK;

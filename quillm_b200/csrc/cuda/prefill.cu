@@ -2,6 +2,7 @@
 // (quantized weights) or gemm_f32; the driver is qmc_model_prefill in model.cu.
 #include <algorithm>
 
+#include "actquant.cuh"
 #include "prefill.cuh"
 
 namespace qmc {
@@ -40,8 +41,11 @@ __global__ void rmsnorm_rows_kernel(const float *__restrict__ x, const float *__
 
 // rmsnorm of one row per block followed by its Q8_0 quantization, without the normalised row in memory:
 // the same operations as rmsnorm_rows then quantize_act (inv from the double sum of squares, v = (x * inv)
-// * w rounded twice, per 32-element block the reference's quantizer), so the blocks are bit-identical
-// With `add`, the row first takes the residual add x += add (written back; src/model.c:179,186).
+// * w rounded twice, per 32-element block the reference's quantizer), so the blocks are bit-identical.
+// With `add`, the row first takes the residual add x += add (written back; src/model.c:179,186).  Four
+// threads per 32-element block, 8 elements each (quant_group<8>), blockDim / 4 blocks a round: a row of
+// one round (n <= 8192 at 1024 threads) keeps its values in registers across the block sum, all loads in
+// flight at once.
 __global__ void rmsnorm_quant_rows_kernel(float *__restrict__ x, const float *__restrict__ add, const float *__restrict__ w,
                                           int64_t n, float eps, int8_t *__restrict__ qs, float *__restrict__ d,
                                           float *__restrict__ dT, int64_t ldT) {
@@ -49,12 +53,27 @@ __global__ void rmsnorm_quant_rows_kernel(float *__restrict__ x, const float *__
     __shared__ float inv_s;
     const int64_t row = blockIdx.x;
     float *xr = x + row * n;
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const float *ar = add ? add + row * n : nullptr;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, j = t & 3;
+    const int qb = blockDim.x >> 2;  // blocks per round
+    const int64_t nb = nblocks(n);
+    const int rounds = (int)((nb + qb - 1) / qb);
+    float v[8];
     double ss = 0.0;
-    for (int64_t i = t; i < n; i += blockDim.x) {
-        float v = xr[i];
-        if (add) xr[i] = v = __fadd_rn(v, add[row * n + i]);
-        ss = fma((double)v, (double)v, ss);
+    for (int r = 0; r < rounds; r++) {
+        const int64_t e0 = ((int64_t)r * qb + (t >> 2)) * 32 + 8 * j;
+        load8_any(xr, e0, n, v);
+        if (ar) {
+            float a[8];
+            load8_any(ar, e0, n, a);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                v[i] = __fadd_rn(v[i], a[i]);
+                if (e0 + i < n) xr[e0 + i] = v[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss = fma((double)v[i], (double)v[i], ss);
     }
     ss = warp_sum_d(ss);
     if (lane == 0) red[warp] = ss;
@@ -66,45 +85,43 @@ __global__ void rmsnorm_quant_rows_kernel(float *__restrict__ x, const float *__
     }
     __syncthreads();
     const float inv = inv_s;
-    const int64_t nb = nblocks(n);
-    for (int64_t b = warp; b < nb; b += blockDim.x >> 5) {
-        const int64_t c = b * 32 + lane;
-        const float v = c < n ? __fmul_rn(__fmul_rn(xr[c], inv), w[c]) : 0.0f;
-        float dd;
-        uint32_t dh;
-        const int q = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
-        qs[row * nb * 32 + c] = (int8_t)q;
-        if (lane == 0) {
-            d[row * nb + b] = dd;
-            if (dT) dT[b * ldT + row] = dd;
+    for (int r = 0; r < rounds; r++) {
+        const int64_t b = (int64_t)r * qb + (t >> 2), e0 = b * 32 + 8 * j;
+        if (rounds > 1) load8_any(xr, e0, n, v);  // this thread's own values (the add written back above)
+        float wv[8];
+        load8_any(w, e0, n, wv);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
+        uint32_t q[2];
+        int sum;
+        float sc;
+        quant_group<8>(v, q, sum, sc);
+        if (b < nb) {
+            *(uint2 *)(qs + (row * nb + b) * 32 + 8 * j) = make_uint2(q[0], q[1]);
+            if (j == 0) {
+                d[row * nb + b] = sc;
+                if (dT) dT[b * ldT + row] = sc;
+            }
         }
     }
 }
 
 // h = silu(g) * u over T rows of n (the SwiGLU of src/ops.c:128-133, same roundings as swiglu_kernel)
-// straight into its Q8_0 blocks: warp per 32-element block, h never stored
+// straight into its Q8_0 blocks (quant_rows_quads), h never stored
 __global__ void swiglu_quant_rows_kernel(const float *__restrict__ g, const float *__restrict__ u, int64_t T, int64_t n,
                                          int8_t *__restrict__ qs, float *__restrict__ d, float *__restrict__ dT,
                                          int64_t ldT) {
-    const int lane = threadIdx.x & 31;
-    const int64_t nb = nblocks(n);
-    const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t blk = w0; blk < T * nb; blk += nw) {
-        const int64_t t = blk / nb, b = blk % nb, c = b * 32 + lane;
-        float v = 0.0f;
-        if (c < n) {
-            const float gv = g[t * n + c];
-            v = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[t * n + c]);
-        }
-        float dd;
-        uint32_t dh;
-        const int q = quant_lane(v, 127.0f, -127, 127, &dd, &dh);
-        qs[t * nb * 32 + c] = (int8_t)q;
-        if (lane == 0) {
-            d[t * nb + b] = dd;
-            if (dT) dT[b * ldT + t] = dd;
-        }
-    }
+    quant_rows_quads(
+        T, n,
+        [&](int64_t t, int64_t e0, float (&v)[8]) {
+            float gv[8], uv[8];
+            load8_any(g + t * n, e0, n, gv);
+            load8_any(u + t * n, e0, n, uv);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                v[i] = e0 + i < n ? __fmul_rn(__fdiv_rn(gv[i], __fadd_rn(1.0f, expf(-gv[i]))), uv[i]) : 0.0f;
+        },
+        qs, d, dT, ldT);
 }
 
 // p0 = x0 c - x1 s ; p1 = x0 s + x1 c, each product and sum rounded separately (src/ops.c:121-123)
@@ -113,22 +130,24 @@ __device__ __forceinline__ void rope_rotate(float a, float b, float2 cs, float &
     o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
 }
 
+// one thread per value pair of a row: RoPE on the q / k pairs (k to its cache slot), v copied to its slot
 __global__ void rope_kv_rows_kernel(float *__restrict__ qkv, int Dq, int KVl, int hd, int pos0,
                                     const float2 *__restrict__ rope, void *__restrict__ kc, void *__restrict__ vc,
                                     bool kv16) {
-    const int64_t t = blockIdx.x;
+    const int64_t t = blockIdx.y;
     const int pos = pos0 + (int)t;
     float *row = qkv + t * (int64_t)(Dq + 2 * KVl);
-    const float2 *cs = rope + (int64_t)pos * (hd >> 1);
-    for (int i = threadIdx.x; i < (Dq + KVl) >> 1; i += blockDim.x) {
+    const int i = (int)blockIdx.x * blockDim.x + threadIdx.x, nrot = (Dq + KVl) >> 1;
+    if (i < nrot) {
         const int e = 2 * i;  // pair (e, e + 1) of q (e < Dq) or k
         float o0, o1;
-        rope_rotate(row[e], row[e + 1], cs[(e % hd) >> 1], o0, o1);
+        rope_rotate(row[e], row[e + 1], rope[(int64_t)pos * (hd >> 1) + ((e % hd) >> 1)], o0, o1);
         if (e < Dq) row[e] = o0, row[e + 1] = o1;
         else kv_st2(kc, kv16, (int64_t)pos * KVl + (e - Dq), o0, o1);
+    } else if (i < nrot + (KVl >> 1)) {
+        const int e = 2 * (i - nrot);
+        kv_st2(vc, kv16, (int64_t)pos * KVl + e, row[Dq + KVl + e], row[Dq + KVl + e + 1]);
     }
-    for (int i = threadIdx.x; i < KVl >> 1; i += blockDim.x)
-        kv_st2(vc, kv16, (int64_t)pos * KVl + 2 * i, row[Dq + KVl + 2 * i], row[Dq + KVl + 2 * i + 1]);
 }
 
 // Causal attention of a tile of kQT query tokens of one head: the head's K and V rows are staged through
@@ -137,7 +156,10 @@ __global__ void rope_kv_rows_kernel(float *__restrict__ qkv, int Dq, int KVl, in
 // memory so lane p reads its own column), the warp updates the online softmax once for the tile (max,
 // one rescale of the running sum and accumulator), and lane l accumulates head dimensions 4l .. 4l + 3
 // over the tile's positions.  Rows are zero-padded to a multiple of 4 dimensions in shared memory.
-constexpr int kQT = 32, kPT = 32;  // query tokens per block, positions per staged tile
+// QT (query tokens per block: 8, 16 or 32) only groups the tokens: every token's arithmetic is the same
+// whatever the tile, so the launch takes the largest tile that still gives every SM two blocks (short
+// prompts run many small tiles, long ones share each staged K/V tile among 32 tokens).
+constexpr int kPT = 32;  // positions per staged tile (one per lane)
 // four consecutive cache elements (16-byte aligned for float, 8-byte for __half)
 __device__ __forceinline__ float4 kv_ld4(const float *p) { return __ldcg((const float4 *)p); }
 __device__ __forceinline__ float4 kv_ld4(const __half *p) {
@@ -145,7 +167,7 @@ __device__ __forceinline__ float4 kv_ld4(const __half *p) {
     const float2 a = __half22float2(*(const __half2 *)&r.x), b = __half22float2(*(const __half2 *)&r.y);
     return make_float4(a.x, a.y, b.x, b.y);
 }
-template <typename KT>             // cache element: float or __half
+template <typename KT, int QT>     // cache element: float or __half; query tokens per block
 __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const float *__restrict__ qkv, int64_t T, int64_t ldq, int group,
                                                            int hd, int KVl, int pos0, float scale,
                                                            const KT *__restrict__ kc, const KT *__restrict__ vc,
@@ -154,16 +176,16 @@ __global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const float *__res
     const int hd4 = (hd + 3) & ~3;
     float *Kt = smf;                 // [hd4 / 4][kPT][4]: dims 4c .. 4c + 3 of position p at (c * kPT + p) * 4
     float *Vs = Kt + hd4 * kPT;      // [kPT][hd4]
-    float *Qs = Vs + kPT * hd4;      // [kQT][hd4]
+    float *Qs = Vs + kPT * hd4;      // [QT][hd4]
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int h = blockIdx.y, kvh = h / group;
-    const int64_t tq0 = (int64_t)blockIdx.x * kQT;
-    const int nq = (int)(T - tq0 < kQT ? T - tq0 : kQT);
-    for (int i = tid; i < kQT * hd4; i += 128) {
+    const int64_t tq0 = (int64_t)blockIdx.x * QT;
+    const int nq = (int)(T - tq0 < QT ? T - tq0 : QT);
+    for (int i = tid; i < QT * hd4; i += 128) {
         const int r = i / hd4, d = i % hd4;
         Qs[i] = (r < nq && d < hd) ? qkv[(tq0 + r) * ldq + (int64_t)h * hd + d] : 0.0f;
     }
-    constexpr int TW = kQT / 4;  // tokens per warp
+    constexpr int TW = QT / 4;  // tokens per warp
     float m[TW], l[TW], o[TW][4];
 #pragma unroll
     for (int j = 0; j < TW; j++) {
@@ -275,15 +297,16 @@ int launch_rmsnorm_rows(const float *x, const float *w, float *out, int64_t T, i
 
 int launch_rmsnorm_quant_rows(float *x, const float *add, const float *w, int64_t T, int64_t n, float eps, int8_t *qs,
                               float *d, float *dT, int64_t ldT, cudaStream_t s) {
-    rmsnorm_quant_rows_kernel<<<(unsigned)T, 256, 0, s>>>(x, add, w, n, eps, qs, d, dT, ldT);
+    // four threads per block: one round up to 8192 elements
+    const int threads = (int)std::min<int64_t>(1024, std::max<int64_t>(32, (nblocks(n) * 4 + 31) / 32 * 32));
+    rmsnorm_quant_rows_kernel<<<(unsigned)T, threads, 0, s>>>(x, add, w, n, eps, qs, d, dT, ldT);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }
 
 int launch_swiglu_quant_rows(const float *g, const float *u, int64_t T, int64_t n, int8_t *qs, float *d, float *dT,
                              int64_t ldT, cudaStream_t s) {
-    const int64_t warps = T * nblocks(n);
-    const int64_t grid = (warps * 32 + 255) / 256;
+    const int64_t grid = (T * nblocks(n) * 4 + 255) / 256;  // a thread per 8 elements (the loop covers the rest)
     swiglu_quant_rows_kernel<<<(int)(grid < 65535 ? grid : 65535), 256, 0, s>>>(g, u, T, n, qs, d, dT, ldT);
     QMC_LAUNCH_CHECK();
     return QMC_OK;
@@ -291,7 +314,34 @@ int launch_swiglu_quant_rows(const float *g, const float *u, int64_t T, int64_t 
 
 int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0, const float2 *rope, void *kc,
                         void *vc, bool kv16, cudaStream_t s) {
-    rope_kv_rows_kernel<<<(unsigned)T, 256, 0, s>>>(qkv, Dq, KVl, hd, pos0, rope, kc, vc, kv16);
+    if (T > 65535) return set_error(QMC_EINVAL, "prefill rope: %lld rows exceed the grid", (long long)T);
+    const int pairs = ((Dq + KVl) >> 1) + (KVl >> 1);
+    rope_kv_rows_kernel<<<dim3((unsigned)((pairs + 255) / 256), (unsigned)T), 256, 0, s>>>(qkv, Dq, KVl, hd, pos0, rope, kc,
+                                                                                         vc, kv16);
+    QMC_LAUNCH_CHECK();
+    return QMC_OK;
+}
+
+template <int QT>
+int launch_attn_prefill_t(const float *qkv, int64_t T, int64_t ldq, int n_heads, int group, int hd, int KVl, int pos0,
+                          float scale, const void *kc, const void *vc, bool kv16, float *out, int dev, cudaStream_t s) {
+    const int hd4 = (hd + 3) & ~3;
+    const size_t smem = (size_t)(hd4 * kPT + kPT * hd4 + QT * hd4) * 4;
+    dim3 grid((unsigned)((T + QT - 1) / QT), (unsigned)n_heads);
+    static bool attr_done[64];
+    if (!attr_done[dev]) {  // the largest tile set (head_dim 128)
+        const int most = (2 * 128 * kPT + QT * 128) * 4;
+        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<__half, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<float, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+        attr_done[dev] = true;
+    }
+    if (kv16) {
+        attn_prefill_kernel<__half, QT><<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale,
+                                                               (const __half *)kc, (const __half *)vc, out);
+    } else {
+        attn_prefill_kernel<float, QT><<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale,
+                                                              (const float *)kc, (const float *)vc, out);
+    }
     QMC_LAUNCH_CHECK();
     return QMC_OK;
 }
@@ -299,28 +349,16 @@ int launch_rope_kv_rows(float *qkv, int64_t T, int Dq, int KVl, int hd, int pos0
 int launch_attn_prefill(const float *qkv, int64_t T, int64_t ldq, int n_heads, int group, int hd, int KVl, int pos0,
                         float scale, const void *kc, const void *vc, bool kv16, float *out, cudaStream_t s) {
     if (hd > 128) return set_error(QMC_EINVAL, "prefill attention: head_dim %d > 128", hd);
-    const int hd4 = (hd + 3) & ~3;
-    const size_t smem = (size_t)(hd4 * kPT + kPT * hd4 + kQT * hd4) * 4;
-    dim3 grid((unsigned)((T + kQT - 1) / kQT), (unsigned)n_heads);
     int dev = 0;
     QMC_CUDA(cudaGetDevice(&dev));
-    static bool attr_done[64];
     if (dev < 0 || dev >= 64) return set_error(QMC_EINVAL, "prefill attention: device %d out of range", dev);
-    if (!attr_done[dev]) {  // the largest tile set (head_dim 128)
-        const int most = 3 * 128 * kPT * 4;
-        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
-        QMC_CUDA(cudaFuncSetAttribute(attn_prefill_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
-        attr_done[dev] = true;
-    }
-    if (kv16) {
-        attn_prefill_kernel<<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const __half *)kc,
-                                                    (const __half *)vc, out);
-    } else {
-        attn_prefill_kernel<<<grid, 128, smem, s>>>(qkv, T, ldq, group, hd, KVl, pos0, scale, (const float *)kc,
-                                                    (const float *)vc, out);
-    }
-    QMC_LAUNCH_CHECK();
-    return QMC_OK;
+    const DevCtx *c = ctx();
+    const int64_t want = 2 * (int64_t)(c ? c->num_sms : 148);  // blocks
+    if ((T + 31) / 32 * n_heads >= want)
+        return launch_attn_prefill_t<32>(qkv, T, ldq, n_heads, group, hd, KVl, pos0, scale, kc, vc, kv16, out, dev, s);
+    if ((T + 15) / 16 * n_heads >= want)
+        return launch_attn_prefill_t<16>(qkv, T, ldq, n_heads, group, hd, KVl, pos0, scale, kc, vc, kv16, out, dev, s);
+    return launch_attn_prefill_t<8>(qkv, T, ldq, n_heads, group, hd, KVl, pos0, scale, kc, vc, kv16, out, dev, s);
 }
 
 int launch_add(float *x, const float *y, int64_t n, cudaStream_t s) {

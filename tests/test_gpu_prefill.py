@@ -67,12 +67,15 @@ def test_prefill_matches_token_at_a_time_reference(cuda_dev, name, tol):
     m.close()
 
 
-def test_prefill_long_prompt_gqa(cuda_dev):
-    """a 61-token prompt on a synthesized GQA model (8 query / 2 KV heads): the prefill's logits and the
-    decode steps after it agree with feeding the prompt token by token"""
-    cfg = dict(dim=256, hidden_dim=688, n_layers=3, n_heads=8, n_kv_heads=2, vocab_size=2000, max_seq=128)
+@pytest.mark.parametrize("heads,kv_heads,n_prompt", [(8, 2, 61), (32, 8, 200), (32, 8, 300)])
+def test_prefill_long_prompt_gqa(cuda_dev, heads, kv_heads, n_prompt):
+    """a long prompt on a synthesized GQA model: the prefill's logits and the decode steps after it agree
+    with feeding the prompt token by token.  On a 148-SM B200 the three cases take the attention kernel's
+    8-, 16- and 32-token query tiles (the largest tile that still gives every SM two blocks)"""
+    cfg = dict(dim=256 if heads == 8 else 512, hidden_dim=688, n_layers=3 if heads == 8 else 2, n_heads=heads,
+               n_kv_heads=kv_heads, vocab_size=2000, max_seq=128 if n_prompt < 100 else 320)
     rng = np.random.default_rng(3)
-    prompt = rng.integers(0, cfg["vocab_size"], 61).astype(np.int32)
+    prompt = rng.integers(0, cfg["vocab_size"], n_prompt).astype(np.int32)
     for dt in (qb.QMC_Q8_0, qb.QMC_Q4_0):
         a = qb.Model(dict(cfg))
         a.synthesize(dt, 21, 0.05)
