@@ -175,7 +175,7 @@ def test_matmul_tensor_core_bitwise_equals_scalar_matvec(cuda_dev, dt):
     and with extreme block scales and saturated int8 values"""
     rng = np.random.default_rng(16)
     shapes = [(1, 64, 64), (8, 300, 288), (33, 130, 1000), (70, 257, 4096), (128, 1024, 512), (31, 128, 96),
-              (200, 384, 4096), (5, 129, 32)]
+              (200, 384, 4096), (5, 129, 32), (512, 4096, 256), (520, 4200, 100)]
     for T, N, K in shapes:
         Wf = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
         A = rng.standard_normal((T, K)).astype(np.float32)
