@@ -134,9 +134,17 @@ __device__ __forceinline__ unsigned long long *trace_stage(const DecodeParams &p
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// 32-bit arithmetic where blockIdx.x * units fits (a 64-bit division is a long software routine on the
+// critical path of every phase)
 __device__ __forceinline__ void split_units(int64_t units, int64_t &u0, int64_t &u1) {
-    u0 = (int64_t)blockIdx.x * units / gridDim.x;
-    u1 = (int64_t)(blockIdx.x + 1) * units / gridDim.x;
+    if (units <= 0xffffff) {
+        const unsigned n = (unsigned)units, b = blockIdx.x;
+        u0 = (int64_t)(b * n / gridDim.x);
+        u1 = (int64_t)((b + 1) * n / gridDim.x);
+    } else {
+        u0 = (int64_t)blockIdx.x * units / gridDim.x;
+        u1 = (int64_t)(blockIdx.x + 1) * units / gridDim.x;
+    }
 }
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {  // unsigned a bytes x signed b bytes
     int d;
@@ -361,7 +369,7 @@ __device__ __forceinline__ const float *attn_part(const DecodeParams &p, int hq,
 __device__ void attn_out16(const DecodeParams &p, int64_t e0, int K, int nseg, float (&v)[16]) {
     const int hd = p.hd;
     if ((hd & 15) == 0 && e0 + 16 <= K && nseg <= kFastSegs) {  // one head, few segments: loads at once
-        const int hq = (int)(e0 / hd), d0 = (int)(e0 % hd);
+        const int hq = (int)e0 / hd, d0 = (int)e0 % hd;  // e0 < K: 32-bit
         const float *head = attn_part(p, hq, 0), *src = head + kPartHead + d0;  // segment 0: (max, sum), acc
         const int64_t sstride = (int64_t)GMAX * (hd + kPartHead);
         float2 ml[kFastSegs];
@@ -404,7 +412,7 @@ __device__ void attn_out16(const DecodeParams &p, int64_t e0, int K, int nseg, f
             v[i] = 0.0f;
             continue;
         }
-        const int hq = (int)(e / hd), d = (int)(e % hd);
+        const int hq = (int)e / hd, d = (int)e % hd;
         float M = -INFINITY, den = 0.0f, num = 0.0f;
         for (int sg = 0; sg < nseg; sg++) {
             const float *src = attn_part(p, hq, sg);
@@ -627,7 +635,7 @@ __device__ __forceinline__ void rope_pair(float a, float b, float2 cs, float &o0
 __device__ __forceinline__ float2 epilogue_operand(const DecodeParams &p, const DecodePhase &ph, int64_t unit, int pos) {
     if (ph.kind == PH_QKV) {
         const int64_t vr = 2 * unit;
-        if (vr < p.Dq + p.KVl) return p.rope[(int64_t)pos * (p.hd >> 1) + (int)((vr % p.hd) >> 1)];
+        if (vr < p.Dq + p.KVl) return p.rope[(int64_t)pos * (p.hd >> 1) + (((int)vr % p.hd) >> 1)];
         return make_float2(0.0f, 0.0f);
     }
     if (ph.kind == PH_WO || ph.kind == PH_W2) return make_float2(__ldcg(ph.out + unit), 0.0f);
